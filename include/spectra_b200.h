@@ -1,0 +1,121 @@
+/*
+ * spectra_b200.h -- C ABI of libspectra_b200.so, the B200 (sm_100a) W4A16
+ * linear-layer hot path of SPECTRA.
+ *
+ * Weight format (produced by the reference's SpectraCompressor,
+ * spectra/compressor.py:72-112, and bound by spectra/engine.py:999-1026):
+ *   packed   u8   [N, K/2]   two 4-bit codes per byte, unit column stride
+ *   scales   fp16 [N, K/32]  one per group of 32 input features
+ *   zeros    u8   [N, K/32]  one zero-point (0..15) per group, unpacked
+ *   outlier_idx  int64|int32 [n_out]     input columns kept exactly
+ *   outlier_w    fp16|bf16  [N, n_out]   their exact weights
+ * dequantised weight:  w[n,k] = (q[n,k] - z[n,k/32]) * s[n,k/32]
+ * Nibble order inside a 32-code group (16 bytes):
+ *   SPECTRA_LAYOUT_MARLIN   byte j: k=j in the low nibble, k=j+16 in the high nibble
+ *   SPECTRA_LAYOUT_EVEN_ODD byte b: k=2b low, k=2b+1 high
+ *
+ * Conventions: every pointer is a device pointer; strides are in ELEMENTS of
+ * the pointed-to type; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Calls never allocate device memory and never synchronise the
+ * host.  All argument checks run on the host before any CUDA call, so a bad
+ * call returns an error code and launches nothing.  Return value: SPECTRA_OK
+ * or one of the SPECTRA_ERR_* codes below.
+ */
+#ifndef SPECTRA_B200_H
+#define SPECTRA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SPECTRA_API __attribute__((visibility("default")))
+#else
+#define SPECTRA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPECTRA_B200_ABI_VERSION 1
+
+/* element types */
+#define SPECTRA_DT_F16  0
+#define SPECTRA_DT_BF16 1
+#define SPECTRA_DT_F32  2
+#define SPECTRA_DT_I32  3
+#define SPECTRA_DT_I64  4
+
+/* nibble order */
+#define SPECTRA_LAYOUT_EVEN_ODD 0
+#define SPECTRA_LAYOUT_MARLIN   1
+
+/* status codes */
+#define SPECTRA_OK               0
+#define SPECTRA_ERR_NULL_POINTER 1
+#define SPECTRA_ERR_SHAPE        2
+#define SPECTRA_ERR_STRIDE       3
+#define SPECTRA_ERR_ALIGNMENT    4
+#define SPECTRA_ERR_DTYPE        5
+#define SPECTRA_ERR_WORKSPACE    6
+#define SPECTRA_ERR_CUDA         7
+#define SPECTRA_ERR_UNSUPPORTED  8
+
+/* Version of this ABI (SPECTRA_B200_ABI_VERSION of the built library). */
+SPECTRA_API int spectra_abi_version(void);
+
+/* Static, NUL-terminated description of a status code. */
+SPECTRA_API const char* spectra_status_string(int status);
+
+/* cudaError_t of the last CUDA call that failed on the calling thread
+ * (0 if none); read it after a call returned SPECTRA_ERR_CUDA. */
+SPECTRA_API int spectra_last_cuda_error(void);
+
+/*
+ * M=1 decode GEMV with fused outlier-column and bias adds.
+ * Replaces spectra/kernels.py:132-184 (fused_w4a16_gemv_hdsq, the wrapper)
+ * and spectra/kernels.py:16-129 (_fused_w4a16_gemv_hdsq_kernel).
+ *   y[n] = sum_k x[k]*w[n,k] + sum_j x[idx_j]*ow[n,j] + bias[n]
+ * accumulated in fp32 and rounded once to y_dtype.
+ *   x      [K]  at x + k*x_stride, x_dtype F16|BF16|F32
+ *   packed row n at packed + n*w_row_stride (bytes); column stride is 1
+ *   scales[n,g] at scales + n*s_row_stride + g*s_col_stride (fp16 bits)
+ *   zeros [n,g] at zeros  + n*z_row_stride + g*z_col_stride
+ *   bias   [N] or NULL (bias_dtype F16|BF16|F32)
+ *   outlier_idx NULL or [n_out] (idx_dtype I32|I64); outlier_w [n,j] at
+ *          outlier_w + n*ow_row_stride + j*ow_col_stride (ow_dtype F16|BF16|F32)
+ *   y      [N]  at y + n*y_stride, y_dtype F16|BF16|F32
+ * K must be a positive multiple of 32 and N positive.
+ */
+SPECTRA_API int spectra_w4a16_gemv(
+    const void* x, int x_dtype, int64_t x_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* bias, int bias_dtype,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* y, int y_dtype, int64_t y_stride,
+    int64_t N, int64_t K, int layout, void* stream);
+
+/*
+ * Dequantise to a dense matrix.  out_dtype F32 gives (q-z)*s exactly (the
+ * fp32 value the reference GEMV multiplies by, spectra/kernels.py:73-74);
+ * BF16 / F16 give that value rounded to nearest-even, the operand the
+ * reference GEMM feeds its tensor-core dot (spectra/kernels.py:256-261).
+ * Outlier columns are left as dequantised (the reference test overwrites
+ * them with outlier_w, tests/test_kernels.py:38-39; that is the caller's job).
+ *   out[n,k] at out + n*out_row_stride + k
+ */
+SPECTRA_API int spectra_w4a16_dequant(
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    void* out, int out_dtype, int64_t out_row_stride,
+    int64_t N, int64_t K, int layout, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* SPECTRA_B200_H */

@@ -1,0 +1,133 @@
+// extern "C" entry points of libspectra_b200.so (declared in
+// include/spectra_b200.h).  Every argument check runs on the host before any
+// CUDA call, so an invalid call returns a status code and launches nothing.
+#include <cstdint>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "gemv.h"
+
+namespace spectra {
+
+namespace {
+thread_local int g_last_cuda_error = 0;
+
+bool is_float_dt(int dt) { return dt == SPECTRA_DT_F16 || dt == SPECTRA_DT_BF16 || dt == SPECTRA_DT_F32; }
+bool is_index_dt(int dt) { return dt == SPECTRA_DT_I32 || dt == SPECTRA_DT_I64; }
+size_t dt_size(int dt) { return (dt == SPECTRA_DT_F16 || dt == SPECTRA_DT_BF16) ? 2 : (dt == SPECTRA_DT_I64 ? 8 : 4); }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool fits_i32(int64_t v) { return v >= 0 && v <= INT32_MAX; }
+
+// Shared checks of the quantised weight tensors.
+int check_weights(const uint8_t* packed, const uint16_t* scales, const uint8_t* zeros,
+                  int64_t N, int64_t K, int layout) {
+  if (!packed || !scales || !zeros) return SPECTRA_ERR_NULL_POINTER;
+  if (N <= 0 || K <= 0 || (K % kGroup) != 0 || !fits_i32(N) || !fits_i32(K)) return SPECTRA_ERR_SHAPE;
+  if (layout != SPECTRA_LAYOUT_MARLIN && layout != SPECTRA_LAYOUT_EVEN_ODD) return SPECTRA_ERR_UNSUPPORTED;
+  if (!aligned(scales, 2)) return SPECTRA_ERR_ALIGNMENT;
+  return SPECTRA_OK;
+}
+}  // namespace
+
+void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = int(e); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SPECTRA_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+bool bulk_path_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SPECTRA_B200_GEMV_BULK");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+}  // namespace spectra
+
+using namespace spectra;
+
+extern "C" {
+
+int spectra_abi_version(void) { return SPECTRA_B200_ABI_VERSION; }
+
+const char* spectra_status_string(int status) {
+  switch (status) {
+    case SPECTRA_OK: return "ok";
+    case SPECTRA_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case SPECTRA_ERR_SHAPE: return "invalid shape (N, K > 0, K a multiple of 32, sizes within int32)";
+    case SPECTRA_ERR_STRIDE: return "invalid stride";
+    case SPECTRA_ERR_ALIGNMENT: return "pointer not aligned to its element size";
+    case SPECTRA_ERR_DTYPE: return "unsupported dtype code";
+    case SPECTRA_ERR_WORKSPACE: return "workspace missing or too small";
+    case SPECTRA_ERR_CUDA: return "CUDA error (see spectra_last_cuda_error)";
+    case SPECTRA_ERR_UNSUPPORTED: return "unsupported argument combination";
+    default: return "unknown status";
+  }
+}
+
+int spectra_last_cuda_error(void) { return g_last_cuda_error; }
+
+int spectra_w4a16_gemv(
+    const void* x, int x_dtype, int64_t x_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* bias, int bias_dtype,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* y, int y_dtype, int64_t y_stride,
+    int64_t N, int64_t K, int layout, void* stream) {
+  int st = check_weights(packed, scales, zeros, N, K, layout);
+  if (st != SPECTRA_OK) return st;
+  if (!x || !y) return SPECTRA_ERR_NULL_POINTER;
+  if (!is_float_dt(x_dtype) || !is_float_dt(y_dtype)) return SPECTRA_ERR_DTYPE;
+  if (bias && !is_float_dt(bias_dtype)) return SPECTRA_ERR_DTYPE;
+  if (n_out < 0 || !fits_i32(n_out)) return SPECTRA_ERR_SHAPE;
+  const bool has_out = n_out > 0 && outlier_idx && outlier_w;
+  if (n_out > 0 && (!outlier_idx || !outlier_w)) return SPECTRA_ERR_NULL_POINTER;
+  if (has_out && (!is_index_dt(idx_dtype) || !is_float_dt(ow_dtype))) return SPECTRA_ERR_DTYPE;
+  if (y_stride == 0 && N > 1) return SPECTRA_ERR_STRIDE;
+  if (!aligned(x, dt_size(x_dtype)) || !aligned(y, dt_size(y_dtype)) ||
+      (bias && !aligned(bias, dt_size(bias_dtype))) ||
+      (has_out && (!aligned(outlier_idx, dt_size(idx_dtype)) || !aligned(outlier_w, dt_size(ow_dtype)))))
+    return SPECTRA_ERR_ALIGNMENT;
+  GemvArgs a;
+  a.x = x; a.x_dtype = x_dtype; a.x_stride = x_stride;
+  a.packed = packed; a.w_rs = w_row_stride;
+  a.scales = reinterpret_cast<const __half*>(scales); a.s_rs = s_row_stride; a.s_cs = s_col_stride;
+  a.zeros = zeros; a.z_rs = z_row_stride; a.z_cs = z_col_stride;
+  a.bias = bias; a.bias_dtype = bias_dtype;
+  a.idx = has_out ? outlier_idx : nullptr; a.idx_dtype = idx_dtype; a.n_out = has_out ? int(n_out) : 0;
+  a.ow = has_out ? outlier_w : nullptr; a.ow_dtype = ow_dtype; a.ow_rs = ow_row_stride; a.ow_cs = ow_col_stride;
+  a.y = y; a.y_dtype = y_dtype; a.y_stride = y_stride;
+  a.N = int(N); a.K = int(K); a.layout = layout;
+  return launch_gemv(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_w4a16_dequant(
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    void* out, int out_dtype, int64_t out_row_stride,
+    int64_t N, int64_t K, int layout, void* stream) {
+  int st = check_weights(packed, scales, zeros, N, K, layout);
+  if (st != SPECTRA_OK) return st;
+  if (!out) return SPECTRA_ERR_NULL_POINTER;
+  if (!is_float_dt(out_dtype)) return SPECTRA_ERR_DTYPE;
+  if (!aligned(out, dt_size(out_dtype))) return SPECTRA_ERR_ALIGNMENT;
+  if (out_row_stride < K && N > 1) return SPECTRA_ERR_STRIDE;
+  DequantArgs a;
+  a.packed = packed; a.w_rs = w_row_stride;
+  a.scales = reinterpret_cast<const __half*>(scales); a.s_rs = s_row_stride; a.s_cs = s_col_stride;
+  a.zeros = zeros; a.z_rs = z_row_stride; a.z_cs = z_col_stride;
+  a.out = out; a.out_dtype = out_dtype; a.out_rs = out_row_stride;
+  a.N = N; a.K = int(K); a.layout = layout;
+  return launch_dequant(a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,95 @@
+// Shared device/host helpers for the W4A16 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "spectra_b200.h"
+
+namespace spectra {
+
+constexpr int kGroup = 32;          // quantisation group (input features)
+constexpr int kGroupBytes = 16;     // packed bytes per group
+constexpr uint32_t kMagic = 0x4B000000u;  // bit pattern of 2^23 in fp32
+constexpr int kMaxDevices = 64;           // per-device launch-attribute caches
+
+// Per-thread record of the last failed CUDA call (exported by
+// spectra_last_cuda_error()).
+void set_last_cuda_error(cudaError_t e);
+
+// Programmatic dependent launch (kernels overlap their weight prefetch with
+// the previous kernel's tail).  On unless SPECTRA_B200_PDL=0 in the environment.
+bool pdl_enabled();
+
+// GEMV main path selection (bulk-copy pipeline unless SPECTRA_B200_GEMV_BULK=0).
+bool bulk_path_enabled();
+
+inline int cuda_status(cudaError_t e) {
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return SPECTRA_ERR_CUDA;
+  }
+  return SPECTRA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// typed scalar loads/stores selected by a runtime dtype code
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_as_float(const void* base, int64_t i, int dt) {
+  if (dt == SPECTRA_DT_BF16) {
+    uint16_t b = __ldg(reinterpret_cast<const unsigned short*>(base) + i);
+    return __uint_as_float(uint32_t(b) << 16);
+  }
+  if (dt == SPECTRA_DT_F16) {
+    return __half2float(__ldg(reinterpret_cast<const __half*>(base) + i));
+  }
+  return __ldg(reinterpret_cast<const float*>(base) + i);
+}
+
+__device__ __forceinline__ int64_t load_index(const void* base, int64_t i, int dt) {
+  if (dt == SPECTRA_DT_I32) return __ldg(reinterpret_cast<const int*>(base) + i);
+  return __ldg(reinterpret_cast<const long long*>(base) + i);
+}
+
+__device__ __forceinline__ void store_from_float(void* base, int64_t i, int dt, float v) {
+  if (dt == SPECTRA_DT_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+  } else if (dt == SPECTRA_DT_F16) {
+    reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);
+  } else {
+    reinterpret_cast<float*>(base)[i] = v;
+  }
+}
+
+// 16 packed bytes (one 32-code group of one row), read once, not kept in L1.
+template <int ALIGN>
+__device__ __forceinline__ uint4 load_group16(const uint8_t* p) {
+  uint4 v;
+  if constexpr (ALIGN >= 16) {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+  } else if constexpr (ALIGN >= 4) {
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+    v.x = __ldg(q + 0); v.y = __ldg(q + 1); v.z = __ldg(q + 2); v.w = __ldg(q + 3);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      w[j] = uint32_t(__ldg(p + 4 * j)) | (uint32_t(__ldg(p + 4 * j + 1)) << 8) |
+             (uint32_t(__ldg(p + 4 * j + 2)) << 16) | (uint32_t(__ldg(p + 4 * j + 3)) << 24);
+    }
+    v = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  return v;
+}
+
+// k offset (0..31) inside its group of the code stored at byte `byte`
+// (0..15), high nibble if `hi`.
+__host__ __device__ __forceinline__ int code_k(int byte, int hi, int layout) {
+  return layout == SPECTRA_LAYOUT_MARLIN ? byte + 16 * hi : 2 * byte + hi;
+}
+
+}  // namespace spectra

@@ -1,0 +1,160 @@
+"""Drop-in replacement of the reference operator module ``spectra.kernels``.
+
+Same names, signatures, argument meaning and return conventions as
+spectra/kernels.py (:132-184 ``fused_w4a16_gemv_hdsq``, :333-389
+``batched_w4a16_gemm``), so ``spectra/engine.py``'s ``SpectraFusedLinear``
+(engine.py:90-124) runs on it unchanged.  Every call goes to the CUDA kernels
+of libspectra_b200.so through the C ABI; there is no CPU, Triton or eager
+PyTorch fallback -- tensors must live on a CUDA device.
+
+Behaviour kept from the reference:
+  * outputs are allocated with ``torch.empty`` on x's device (capture-safe);
+  * the GEMV accumulates exactly-dequantised fp32 weights and rounds once to
+    bf16 when x is bf16, else to fp16 (kernels.py:126-129), then stores into
+    ``out``'s dtype;
+  * the GEMM rounds dequantised weights, activations and outlier weights to
+    the compute dtype (bf16 if ``a`` is bf16 else fp16) and returns
+    ``c.to(a.dtype)`` (kernels.py:347-389); it adds no bias (the engine adds it);
+  * strided views (offloader slots, engine.py:555-569) are accepted.
+Deliberate difference: the reference GEMV computes only row 0 of a [B,K]
+input and leaves rows 1.. of ``out`` unwritten; here every row is computed.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float16: L.DT_F16, torch.bfloat16: L.DT_BF16, torch.float32: L.DT_F32,
+       torch.int32: L.DT_I32, torch.int64: L.DT_I64}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _require_cuda(name: str, t: Optional[torch.Tensor], dev: torch.device) -> None:
+    if t is None:
+        return
+    if not t.is_cuda:
+        raise RuntimeError(f"spectra_b200: {name} must be a CUDA tensor (no CPU fallback), got {t.device}")
+    if t.device != dev:
+        raise RuntimeError(f"spectra_b200: {name} is on {t.device}, expected {dev}")
+
+
+def _unit_cols(t: torch.Tensor) -> torch.Tensor:
+    """Packed codes are read as 16-byte vectors along a row: unit column stride."""
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _weights(packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor):
+    if packed.dtype != torch.uint8 or zeros.dtype != torch.uint8:
+        raise TypeError("packed weights and zero-points must be uint8")
+    if scales.dtype != torch.float16:
+        raise TypeError("scales must be float16")
+    if packed.dim() != 2 or scales.dim() != 2 or zeros.dim() != 2:
+        raise ValueError("packed, scales and zeros must be 2-D")
+    return _unit_cols(packed), scales, zeros
+
+
+def _outliers(outlier_idx, outlier_w, N: int):
+    if outlier_idx is None or outlier_w is None or outlier_idx.numel() == 0:
+        return None, None, 0
+    idx = outlier_idx.reshape(-1)
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.to(torch.int64)
+    if idx.stride(0) != 1:
+        idx = idx.contiguous()
+    ow = outlier_w
+    if ow.dim() != 2 or ow.shape[0] != N or ow.shape[1] != idx.numel():
+        raise ValueError(f"outlier_w must be [N, n_out] = [{N}, {idx.numel()}], got {tuple(ow.shape)}")
+    return idx, ow, idx.numel()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _gemv_row(x_row, packed, scales, zeros, bias, idx, ow, n_out, y_row, layout, N, K, stream):
+    lib = L.lib()
+    st = lib.spectra_w4a16_gemv(
+        x_row.data_ptr(), _dt(x_row), x_row.stride(-1),
+        packed.data_ptr(), packed.stride(0),
+        scales.data_ptr(), scales.stride(0), scales.stride(1),
+        zeros.data_ptr(), zeros.stride(0), zeros.stride(1),
+        bias.data_ptr() if bias is not None else None, _dt(bias) if bias is not None else 0,
+        idx.data_ptr() if idx is not None else None, _dt(idx) if idx is not None else 0, n_out,
+        ow.data_ptr() if ow is not None else None, _dt(ow) if ow is not None else 0,
+        ow.stride(0) if ow is not None else 0, ow.stride(1) if ow is not None else 0,
+        y_row.data_ptr(), _dt(y_row), y_row.stride(-1),
+        N, K, layout, stream)
+    L.check("spectra_w4a16_gemv", st)
+
+
+def fused_w4a16_gemv_hdsq(
+    x: torch.Tensor,
+    packed_w: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    outlier_idx: Optional[torch.Tensor] = None,
+    outlier_w: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    marlin_layout: bool = False,
+) -> torch.Tensor:
+    """M=1 W4A16 GEMV with fused outlier and bias adds (spectra/kernels.py:132-184)."""
+    orig_dim = x.ndim
+    if orig_dim == 1:
+        x = x.unsqueeze(0)
+    B, K = x.shape
+    N = packed_w.shape[0]
+    dev = x.device
+    for name, t in (("packed_w", packed_w), ("scales", scales), ("zeros", zeros), ("bias", bias),
+                    ("outlier_idx", outlier_idx), ("outlier_w", outlier_w), ("out", out)):
+        _require_cuda(name, t, dev)
+    packed, scales, zeros = _weights(packed_w, scales, zeros)
+    idx, ow, n_out = _outliers(outlier_idx, outlier_w, N)
+    if bias is not None and bias.stride(-1) != 1:
+        bias = bias.contiguous()
+    if out is None:
+        out = torch.empty((B, N), device=dev, dtype=x.dtype)
+    # The reference rounds to bf16 for bf16 x, else fp16, then stores into out's dtype.
+    compute = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float16
+    y = out if out.dtype == compute else torch.empty((B, N), device=dev, dtype=compute)
+    layout = L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD
+    with torch.cuda.device(dev):
+        stream = _stream(dev)
+        for b in range(B):
+            _gemv_row(x[b], packed, scales, zeros, bias, idx, ow, n_out, y[b], layout, N, K, stream)
+    if y is not out:
+        out.copy_(y)
+    if orig_dim == 1:
+        out = out.squeeze(0)
+    return out
+
+
+def dequantize(packed_w: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+               marlin_layout: bool = False, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Dense ``(q - z) * s`` on the GPU: exact in fp32, or rounded to nearest-even
+    in bf16/fp16 (the reference GEMM's operand, spectra/kernels.py:256-261)."""
+    dev = packed_w.device
+    for name, t in (("scales", scales), ("zeros", zeros)):
+        _require_cuda(name, t, dev)
+    _require_cuda("packed_w", packed_w, dev)
+    packed, scales, zeros = _weights(packed_w, scales, zeros)
+    N, K = packed.shape[0], packed.shape[1] * 2
+    out = torch.empty((N, K), device=dev, dtype=dtype)
+    with torch.cuda.device(dev):
+        st = L.lib().spectra_w4a16_dequant(
+            packed.data_ptr(), packed.stride(0),
+            scales.data_ptr(), scales.stride(0), scales.stride(1),
+            zeros.data_ptr(), zeros.stride(0), zeros.stride(1),
+            out.data_ptr(), _dt(out), out.stride(0),
+            N, K, L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD, _stream(dev))
+    L.check("spectra_w4a16_dequant", st)
+    return out
