@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark of the W4A16 linear-layer hot path on B200.
+
+Workload: the seven linears of a Llama-3.2-1B decoder
+layer -- q (2048->2048), k, v (2048->512), o (2048->2048), gate, up
+(2048->8192), down (8192->2048) -- at M=1 (decode), bf16 activations, weights
+random N(0, 0.02) fp16 quantised on the device by ``spectra_b200.compress``
+(SPECTRA's group-32 INT4 + outlier-column format, Marlin order).
+
+  step  = the 7 GEMVs of one layer; steps rotate over 8 distinct layer weight
+          copies (8 x 38.8 MB > 2 x the 126 MB L2), so no step reads weights
+          from L2.
+  value = algorithmic bytes of the timed steps / device time (GB/s), weights
+          resident in HBM, steps replayed from CUDA graphs.
+  e2e   = same metric through the public API ``fused_w4a16_gemv_hdsq`` with
+          the step's activations copied from pinned host memory and all seven
+          outputs copied back, every step, inside the timed region.
+
+``--impl reference`` times the reference's CPU formula for the same layer
+(``oracle/cpu_path.py``) on the host cores instead.  Under torchrun (N>1) every
+rank runs the same single-GPU workload on its own layer copies (replicas:
+weak scaling, no collective on the data path) and the slowest rank's time
+counts; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# (name, K, N) of one Llama-3.2-1B decoder layer; input of each linear
+LAYER = [("q_proj", 2048, 2048), ("k_proj", 2048, 512), ("v_proj", 2048, 512), ("o_proj", 2048, 2048),
+         ("gate_proj", 2048, 8192), ("up_proj", 2048, 8192), ("down_proj", 8192, 2048)]
+INPUT_OF = {"q_proj": "h", "k_proj": "h", "v_proj": "h", "o_proj": "attn", "gate_proj": "h", "up_proj": "h",
+            "down_proj": "mlp"}
+INPUT_K = {"h": 2048, "attn": 2048, "mlp": 8192}
+N_COPIES = 8
+METRIC = "W4A16 GEMV GB/s at M=1 (Llama-3.2-1B decoder layer q/k/v/o/gate/up/down)"
+WORKLOAD = "Llama-3.2-1B decoder layer, 7 linears at M=1, bf16 activations"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(M: int, N: int, K: int, n_out: int, act_bytes: int = 2) -> int:
+    """packed codes + fp16 scales + u8 zero points + outlier weights (2 B) and
+    int64 indices + activations in + outputs out."""
+    return (N * K // 2 + 2 * N * K // 32 + N * K // 32 + 2 * N * n_out + 8 * n_out
+            + act_bytes * M * K + act_bytes * M * N)
+
+
+def outlier_count(K: int) -> int:
+    """n_out the reference compressor picks for N(0, 0.02) weights (ratio 0.01..)."""
+    return max(1, int(round(K * 0.01)))
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float) -> dict:
+        inside = [p for (t, p) in self.samples if t0 <= t <= t1]
+        window = "timed region"
+        if not inside:  # region shorter than the sampling period: nearest samples
+            inside = [p for (t, p) in self.samples if t0 - 0.25 <= t <= t1 + 0.25]
+            window = "timed region +-0.25 s"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(p[0]) for p in inside if num(p[0]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in inside for i in range(4) if p[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(inside[0][1]),
+                "reasons": reasons, "samples": len(inside), "window": window,
+                "power_w_max": max((num(p[2]) or 0.0) for p in inside)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+def build_layers(dev, seed: int):
+    """N_COPIES layer weight sets, quantised on the device."""
+    from spectra_b200 import compress as C
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers = []
+    for _ in range(N_COPIES):
+        lay = {}
+        for name, K, N in LAYER:
+            w = (torch.randn(N, K, generator=g, device=dev, dtype=torch.float32) * 0.02).to(torch.float16)
+            c = C.compress_linear(w)
+            del w
+            lay[name] = (c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w)
+        layers.append(lay)
+    return layers
+
+
+def layer_bytes(lay) -> int:
+    return sum(algorithmic_bytes(1, N, K, lay[name][3].numel()) for name, K, N in LAYER)
+
+
+def make_inputs(dev, seed: int):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return {k: torch.randn(1, n, generator=g, device=dev).to(torch.bfloat16) for k, n in INPUT_K.items()}
+
+
+def run_layer(SK, lay, inp, outs):
+    for name, K, N in LAYER:
+        p, s, z, idx, ow = lay[name]
+        SK.fused_w4a16_gemv_hdsq(inp[INPUT_OF[name]], p, s, z, outlier_idx=idx, outlier_w=ow,
+                                 out=outs[name], marlin_layout=True)
+
+
+def capture(fn, dev):
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    return g
+
+
+def time_events(fn, dev) -> float:
+    """Seconds of device time for fn(), CUDA events on the current stream."""
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream(dev)
+    a.record(st)
+    fn()
+    b.record(st)
+    b.synchronize()
+    return a.elapsed_time(b) / 1e3
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU path (reference formula) -- baseline only
+# ---------------------------------------------------------------------------
+
+def cpu_layer_sample(lay_cpu, rows_frac: float, xs):
+    """One step of the CPU formula on the first rows_frac of every linear's rows.
+    Returns (bytes processed, seconds)."""
+    from oracle import cpu_path
+    nbytes = 0
+    t0 = time.perf_counter()
+    for name, K, N in LAYER:
+        p, s, z, idx, ow = lay_cpu[name]
+        n = max(1, int(N * rows_frac))
+        cpu_path.linear(xs[INPUT_OF[name]], p[:n], s[:n], z[:n], idx, ow[:n], marlin=True)
+        nbytes += algorithmic_bytes(1, n, K, idx.numel())
+    return nbytes, time.perf_counter() - t0
+
+
+def cpu_layer_weights(seed: int):
+    from spectra_b200 import compress as C
+    g = torch.Generator().manual_seed(seed)
+    lay = {}
+    for name, K, N in LAYER:
+        w = (torch.randn(N, K, generator=g) * 0.02).to(torch.float16)
+        c = C.compress_linear(w)
+        lay[name] = (c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w)
+    xs = {k: torch.randn(1, n, generator=g).to(torch.bfloat16) for k, n in INPUT_K.items()}
+    return lay, xs
+
+
+def cpu_baseline(budget_s: float = 12.0) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lay, xs = cpu_layer_weights(1234)
+    cpu_layer_sample(lay, 1.0, xs)  # warm-up (allocator, BLAS threads)
+    total_b, total_t, steps = 0, 0.0, 0
+    while total_t < budget_s and steps < 50:
+        b, t = cpu_layer_sample(lay, 1.0, xs)
+        total_b += b
+        total_t += t
+        steps += 1
+    return {"value": total_b / total_t / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} full layer steps (7 linears, all rows) of the reference's CPU formula "
+                      f"(torch dequant + fp32 matmul, oracle/cpu_path.py), {total_t:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU formula on the host cores."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lay, xs = cpu_layer_weights(1234)
+    _, t_full = cpu_layer_sample(lay, 1.0, xs)
+    # bounded sample: the whole run (warm-up + timed steps) within ~90 s
+    per_step = 90.0 / max(1, args.steps + args.warmup)
+    frac = min(1.0, per_step / max(t_full, 1e-6))
+    for _ in range(args.warmup):
+        cpu_layer_sample(lay, frac, xs)
+    nbytes, secs = 0, 0.0
+    for _ in range(args.steps):
+        b, t = cpu_layer_sample(lay, frac, xs)
+        nbytes += b
+        secs += t
+    v = nbytes / secs / 1e9
+    sample = (f"each step: the first {frac * 100:.2f}% of the rows of all 7 linears "
+              f"through the reference's CPU formula (oracle/cpu_path.py)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised by the compressor algorithm; N(0,1) activations)",
+            "config": {"workload": WORKLOAD},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# main arm
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, world, rank, local):
+    from spectra_b200 import kernels as SK
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers = build_layers(dev, seed=17 + 1000 * rank)
+    inp = make_inputs(dev, seed=99 + rank)
+    outs = [{name: torch.empty(1, N, device=dev, dtype=torch.bfloat16) for name, K, N in LAYER}
+            for _ in range(N_COPIES)]
+    bytes_step = layer_bytes(layers[0])
+
+    # graphs: one per layer copy (one step) and one full cycle of N_COPIES steps
+    singles = [capture(lambda l=l: run_layer(SK, layers[l], inp, outs[l]), dev) for l in range(N_COPIES)]
+    cycle = capture(lambda: [run_layer(SK, layers[l], inp, outs[l]) for l in range(N_COPIES)], dev)
+
+    def steps(n, start=0):
+        full, rem = divmod(n, N_COPIES)
+        for _ in range(full):
+            cycle.replay()
+        for i in range(rem):
+            singles[(start + i) % N_COPIES].replay()
+
+    steps(args.warmup)
+    torch.cuda.synchronize(dev)
+
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    w0 = time.time()
+    dt = time_events(lambda: steps(args.steps), dev)
+    w1 = time.time()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    dt_max = max_over_ranks(dt, world, dev)
+    value = bytes_step * args.steps * world / dt_max / 1e9
+
+    # dominant kernel alone: gate_proj GEMV (10.3 MB per launch), rotating copies
+    gate = [layers[l]["gate_proj"] for l in range(N_COPIES)]
+    g_in, g_outs = inp["h"], [outs[l]["gate_proj"] for l in range(N_COPIES)]
+
+    def gate_all():
+        for l in range(N_COPIES):
+            p, s, z, idx, ow = gate[l]
+            SK.fused_w4a16_gemv_hdsq(g_in, p, s, z, outlier_idx=idx, outlier_w=ow, out=g_outs[l], marlin_layout=True)
+    g_gate = capture(gate_all, dev)
+    reps = max(8, 800 // N_COPIES)
+    for _ in range(3):
+        g_gate.replay()
+    dt_gate = time_events(lambda: [g_gate.replay() for _ in range(reps)], dev) / (reps * N_COPIES)
+    clk.stop()
+    gate_bytes = algorithmic_bytes(1, 8192, 2048, gate[0][3].numel())
+    peak, peak_kind = measured_peaks()
+    achieved = gate_bytes / dt_gate / 1e9
+
+    # e2e through the public API with pinned host buffers
+    h_in = {k: v.cpu().pin_memory() for k, v in inp.items()}
+    d_in = {k: torch.empty_like(v) for k, v in inp.items()}
+    h_out = {name: torch.empty(1, N, dtype=torch.bfloat16).pin_memory() for name, K, N in LAYER}
+    h2d = sum(v.numel() * v.element_size() for v in h_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in h_out.values())
+
+    def e2e_steps(n):
+        for i in range(n):
+            lay = layers[i % N_COPIES]
+            for k in d_in:
+                d_in[k].copy_(h_in[k], non_blocking=True)
+            for name, K, N in LAYER:
+                p, s, z, idx, ow = lay[name]
+                y = SK.fused_w4a16_gemv_hdsq(d_in[INPUT_OF[name]], p, s, z, outlier_idx=idx, outlier_w=ow,
+                                             marlin_layout=True)
+                h_out[name].copy_(y, non_blocking=True)
+    e2e_steps(max(3, args.warmup))
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    dt_e2e = time_events(lambda: e2e_steps(args.steps), dev)
+    barrier(world)
+    dt_e2e = max_over_ranks(dt_e2e, world, dev)
+    e2e_value = bytes_step * args.steps * world / dt_e2e / 1e9
+
+    cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,0.02) fp16 weights quantised on device by spectra_b200.compress "
+                    "(SPECTRA group-32 INT4 + outlier columns); N(0,1) bf16 activations",
+            "config": {"workload": WORKLOAD, "bytes_per_step": bytes_step, "layer_weight_copies": N_COPIES,
+                       "l2": f"weights rotated over {N_COPIES} distinct layer copies "
+                             f"({N_COPIES * bytes_step / 1e6:.0f} MB > 2 x 126 MB L2)",
+                       "graphs": "each step replayed from a CUDA graph (programmatic dependent launch edges)",
+                       "parallelism": f"replicas x{world}"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 7 * args.steps * 2,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "GEMV gate_proj K=2048 N=8192 M=1", "peak_source": peak_kind,
+                         "avg_launch_us": round(dt_gate * 1e6, 3)},
+            "clocks": clk.summary(w0, w1),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for g in singles + [cycle, g_gate]:
+        del g
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_gpu(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -39,9 +39,9 @@ bool pdl_enabled() {
   return on;
 }
 
-bool bulk_path_enabled() {
+bool mma_path_enabled() {
   static const bool on = [] {
-    const char* v = std::getenv("SPECTRA_B200_GEMV_BULK");
+    const char* v = std::getenv("SPECTRA_B200_GEMV_MMA");
     return !(v && v[0] == '0');
   }();
   return on;

@@ -23,8 +23,10 @@ void set_last_cuda_error(cudaError_t e);
 // the previous kernel's tail).  On unless SPECTRA_B200_PDL=0 in the environment.
 bool pdl_enabled();
 
-// GEMV main path selection (bulk-copy pipeline unless SPECTRA_B200_GEMV_BULK=0).
-bool bulk_path_enabled();
+
+// M=1 GEMV tensor-core path for bf16/fp16 activations (on unless
+// SPECTRA_B200_GEMV_MMA=0, which selects the exact CUDA-core kernel).
+bool mma_path_enabled();
 
 inline int cuda_status(cudaError_t e) {
   if (e != cudaSuccess) {

@@ -40,16 +40,14 @@ struct GemvKParams {
   int S, RG, win_groups;
   bool vec_x;          // x contiguous, 16-byte aligned, fp16/bf16
   int rows_max;        // max rows of one CTA (bulk kernel)
-  int off_bars, off_xs, off_xsum, off_xos, off_red;  // bulk kernel smem layout
-  int red_passes;      // passes over all of K (bulk kernel partial-sum slots)
-  int off_ow;          // bulk kernel: shared copy of this CTA's outlier-weight rows (-1: not staged)
+  int off_xs, off_xsum, off_xos, off_red;  // dynamic shared-memory layout
+  int red_passes;      // partial-sum slots per row (passes or 8-group blocks of K)
+  int off_ow;          // shared copy of this CTA's outlier-weight rows (-1: not staged)
   int smem_xs_floats;  // win_groups * kXpStride
 };
 
-// slot s = j*8 + i*2 + h of a staged group <-> code of word j (bytes 4j..4j+3),
-// half-word h, nibble i inside that half-word.
-__device__ __forceinline__ int slot_byte(int s) { return 4 * (s >> 3) + 2 * (s & 1) + (((s >> 1) & 3) >> 1); }
-__device__ __forceinline__ int slot_hi(int s) { return (s >> 1) & 1; }
+// Staged-x slot s = j*8 + i*2 + h of a group holds the code of word j
+// (bytes 4j..4j+3), half-word h, nibble i inside that half-word.
 __device__ __forceinline__ float slot_scale(int s) {
   const int i = (s >> 1) & 3;
   return i == 0 ? 1.0f : (i == 1 ? 0.0625f : (i == 2 ? 0.00390625f : 0.000244140625f));
@@ -220,190 +218,6 @@ __device__ __forceinline__ void stage_x_window(const GemvArgs& p, bool vec_x, fl
     }
 }
 
-// Persistent kernel: CTA b owns the contiguous rows [N*b/grid, N*(b+1)/grid),
-// processed in tiles of RG*R rows.  x is staged once per CTA and K-window.
-template <int R, int ALIGN>
-__global__ void __launch_bounds__(256, 2) gemv_w4a16_kernel(const __grid_constant__ GemvKParams kp) {
-  const GemvArgs& p = kp.a;
-  extern __shared__ __align__(16) float smem[];
-  const int rows_cta = kp.RG * R;
-  float* xs = smem;                                   // [win_groups][36]
-  float* xsum = xs + kp.smem_xs_floats;               // [win_groups]
-  float* xos = xsum + kp.win_groups;                  // [n_out]
-  float* red = xos + ((p.n_out + 3) & ~3);            // [2][S][rows_cta]
-  float* acc_rows = red + 2 * kp.S * rows_cta;        // [max_tiles][rows_cta] (multi-window K only)
-
-  // Only weights are read before griddepcontrol.wait; let the next kernel in
-  // the stream start its own weight prefetch as soon as SMs free up.
-  griddep_launch_dependents();
-
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int nthreads = blockDim.x;
-  const int S = kp.S;
-  const int ks = warp % S;
-  const int rg = warp / S;
-  const int G = p.K / kGroup;
-  const int64_t r_begin = (int64_t(p.N) * blockIdx.x) / gridDim.x;
-  const int64_t r_end = (int64_t(p.N) * (blockIdx.x + 1)) / gridDim.x;
-  const int ntiles = int((r_end - r_begin + rows_cta - 1) / rows_cta);
-
-  uint32_t magic_reg;
-  asm volatile("mov.b32 %0, 0x4B000000;" : "=r"(magic_reg));
-
-  // Weight registers of the unit being computed (cur) and of the next unit
-  // (nxt), loaded one unit ahead so a warp always has a load batch in flight.
-  uint4 nw[R];
-  float ns[R], nz[R];
-  auto load_unit = [&](int t, int g_first, int wgn, int pp) {
-    const int gl = pp * 32 + lane;
-    const int g = g_first + gl;
-    const bool gv = gl < wgn;
-    const int64_t row0 = r_begin + int64_t(t) * rows_cta + rg * R;
-    const uint8_t* wp = p.packed + row0 * p.w_rs + int64_t(g) * kGroupBytes;
-    const __half* sp = p.scales + row0 * p.s_rs + int64_t(g) * p.s_cs;
-    const uint8_t* zp = p.zeros + row0 * p.z_rs + int64_t(g) * p.z_cs;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (gv && row0 + r < r_end) {
-        nw[r] = load_group16<ALIGN>(wp + r * p.w_rs);
-        ns[r] = __half2float(__ldg(sp + r * p.s_rs));
-        // u8 -> float with the same magic (ALU) instead of an I2F conversion
-        nz[r] = __uint_as_float(uint32_t(__ldg(zp + r * p.z_rs)) | kMagic) - 8388608.0f;
-      } else {
-        nw[r] = make_uint4(0u, 0u, 0u, 0u);
-        ns[r] = 0.f;
-        nz[r] = 0.f;
-      }
-    }
-  };
-
-  if (ntiles > 0) load_unit(0, 0, min(kp.win_groups, G), ks);
-
-  // Outlier column indices are weights-side data: read them before the wait.
-  constexpr int kOutPerThread = 4;
-  int64_t oidx[kOutPerThread];
-#pragma unroll
-  for (int m = 0; m < kOutPerThread; ++m) {
-    const int j = tid + m * nthreads;
-    oidx[m] = (j < p.n_out) ? load_index(p.idx, j, p.idx_dtype) : -1;
-  }
-
-  griddep_wait();  // x (and the output buffer) belong to the previous kernel
-
-#pragma unroll
-  for (int m = 0; m < kOutPerThread; ++m) {
-    const int j = tid + m * nthreads;
-    if (j < p.n_out) xos[j] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_as_float(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0.f;
-  }
-  for (int j = tid + kOutPerThread * nthreads; j < p.n_out; j += nthreads) {
-    const int64_t k = load_index(p.idx, j, p.idx_dtype);
-    xos[j] = (k >= 0 && k < p.K) ? load_as_float(p.x, k * p.x_stride, p.x_dtype) : 0.f;
-  }
-
-  const bool vec_x = kp.vec_x;
-
-  int buf = 0;
-  const int nwin = (G + kp.win_groups - 1) / kp.win_groups;
-  for (int w = 0; w < nwin; ++w) {
-    const int wg0 = w * kp.win_groups;
-    const int wgn = min(kp.win_groups, G - wg0);
-    if (w > 0) __syncthreads();  // every tile is done with the previous window
-    stage_x_window(p, vec_x, xs, xsum, wg0, wgn, tid, nthreads, lane);
-    __syncthreads();
-
-    const int wpass = (wgn + 31) / 32;
-    if (w > 0 && ntiles > 0) load_unit(0, wg0, wgn, ks);
-    const bool last_win = (w == nwin - 1);
-    for (int t = 0; t < ntiles; ++t) {
-      float acc[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = 0.f;
-      for (int pp = ks; pp < wpass; pp += S) {
-        uint4 cw[R];
-        float cs[R], cz[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) { cw[r] = nw[r]; cs[r] = ns[r]; cz[r] = nz[r]; }
-        // Prefetch the next unit of work before computing this one.
-        if (pp + S < wpass) load_unit(t, wg0, wgn, pp + S);
-        else if (t + 1 < ntiles) load_unit(t + 1, wg0, wgn, ks);
-        const int gl = pp * 32 + lane;
-        if (gl < wgn) {
-          float2 xr[16];
-          const float4* src = reinterpret_cast<const float4*>(xs + gl * kXpStride);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float4 f = src[c];
-            xr[2 * c] = make_float2(f.x, f.y);
-            xr[2 * c + 1] = make_float2(f.z, f.w);
-          }
-          const float xg = xsum[gl];
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float q = group_qdot(cw[r], xr, magic_reg);
-            q = fmaf(-cz[r], xg, q);
-            acc[r] = fmaf(q, cs[r], acc[r]);
-          }
-        }
-      }
-      const int64_t row0 = r_begin + int64_t(t) * rows_cta + rg * R;
-      if (last_win) {
-        // Outlier columns: chunk c of 32 columns is handled by k-split warp c % S.
-        const int nch = (p.n_out + 31) / 32;
-        for (int c = ks; c < nch; c += S) {
-          const int j = c * 32 + lane;
-          if (j < p.n_out) {
-            const float xo = xos[j];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-              const int64_t row = row0 + r;
-              if (row < r_end)
-                acc[r] = fmaf(xo, load_as_float(p.ow, row * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype), acc[r]);
-            }
-          }
-        }
-      }
-      warp_transpose_reduce<R>(acc, lane);
-      constexpr int kLeaderMask = (32 / R) - 1;
-      float* rb = red + buf * S * rows_cta;
-      if ((lane & kLeaderMask) == 0) rb[ks * rows_cta + rg * R + reduced_row<R>(lane)] = acc[0];
-      __syncthreads();
-      for (int i = tid; i < rows_cta; i += nthreads) {
-        const int64_t row = r_begin + int64_t(t) * rows_cta + i;
-        float v = 0.f;
-        for (int q = 0; q < S; ++q) v += rb[q * rows_cta + i];
-        if (nwin > 1) {
-          if (w > 0) v += acc_rows[t * rows_cta + i];
-          if (!last_win) {
-            acc_rows[t * rows_cta + i] = v;
-            continue;
-          }
-        }
-        if (row < r_end) {
-          if (p.bias) v += load_as_float(p.bias, row, p.bias_dtype);
-          store_from_float(p.y, row * p.y_stride, p.y_dtype, v);
-        }
-      }
-      buf ^= 1;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Bulk-copy pipeline (main path).
-//
-// Each warp owns a ring of kBulkStages shared-memory stages.  A stage holds
-// one unit of work -- R rows x one pass (32 groups): 512 packed bytes, 64
-// scale bytes and 32 zero bytes per row -- filled by cp.async.bulk (the TMA
-// engine's non-tensor copy) issued by lane 0 and completed on an mbarrier.
-// Bytes in flight are bounded by shared memory, not registers, and the warp
-// never waits on a CTA barrier inside the main loop: partial sums of each
-// (k-split, row) go to shared memory once per row batch and are combined
-// after a single barrier at the end.
-// ---------------------------------------------------------------------------
-constexpr int kBulkStages = 4;
-
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -413,19 +227,32 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 __device__ int g_gemv_timeouts;  // stuck pipeline waits since load (diagnostic)
 
-template <int R>
-__global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant__ GemvKParams kp) {
+inline int device_sms(int dev) {
+  static int sms[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (sms[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    sms[dev] = v;
+  }
+  return sms[dev];
+}
+
+// ---------------------------------------------------------------------------
+// Rows kernel (main path).
+//
+// Warp (ks, rg) of a CTA owns passes ks, ks+S, ... of each K-window and the
+// rows of row-group rg.  For each of its passes it loads the staged x of its
+// lane's group into registers once, then streams every row of its row-group
+// in batches of R rows, keeping the next batch's loads in flight.  The
+// per-(pass, row) partial sums go to shared memory; one barrier at the end
+// precedes the fixed-order sum over passes (deterministic).
+// ---------------------------------------------------------------------------
+template <int R, int ALIGN>
+__global__ void __launch_bounds__(256, 2) gemv_rows_kernel(const __grid_constant__ GemvKParams kp) {
   using namespace sm100;
   const GemvArgs& p = kp.a;
-  constexpr int kStageBytes = R * (512 + 64 + 32);
-  constexpr int kWarps = 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int nstages = kp.S;  // ring depth of each warp
-  uint8_t* my_stages = smem_raw + size_t(warp) * nstages * kStageBytes;
-  uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem_raw + kp.off_bars) + warp * nstages;
   float* xs = reinterpret_cast<float*>(smem_raw + kp.off_xs);
   float* xsum = reinterpret_cast<float*>(smem_raw + kp.off_xsum);
   float* xos = reinterpret_cast<float*>(smem_raw + kp.off_xos);
@@ -436,21 +263,24 @@ __global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant
 
   griddep_launch_dependents();
 
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int S = kp.S;
+  const int ks = warp % S;
+  const int rg = warp / S;
   const int64_t r_begin = (int64_t(p.N) * blockIdx.x) / gridDim.x;
   const int64_t r_end = (int64_t(p.N) * (blockIdx.x + 1)) / gridDim.x;
   const int nrows = int(r_end - r_begin);
-  const int nb = (nrows + R - 1) / R;
+  const int gb = (nrows * rg) / kp.RG;        // row-group rows, relative to r_begin
+  const int ge = (nrows * (rg + 1)) / kp.RG;
   const int G = p.K / kGroup;
 
   if (tid == 0) s_abort = 0;
-  if (lane == 0) {
-    for (int i = 0; i < nstages; ++i) mbar_init(my_bars + i, 1);
-    fence_mbar_init();
-  }
   for (int i = tid; i < (kp.red_passes + 1) * kp.rows_max; i += blockDim.x) red[i] = 0.f;
-  // This CTA's outlier-weight rows are one contiguous byte range: bring its
-  // 16-byte-aligned body over with one bulk copy now (weights-side data, no
-  // dependency on the previous kernel) and read the ragged tail directly.
+
+  // Outlier-weight rows of this CTA: one bulk copy of the aligned body.
   const int ow_es = p.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   const bool ow_staged = kp.off_ow >= 0 && p.n_out > 0;
   const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
@@ -465,64 +295,36 @@ __global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant
     mbar_arrive_expect_tx(&s_ow_bar, uint32_t(ow_a1 - ow_a0));
     if (ow_a1 > ow_a0) bulk_g2s(ow_smem, ow_src + ow_a0, uint32_t(ow_a1 - ow_a0), &s_ow_bar);
   }
-  __syncwarp();
 
-  // Copy roles of the lanes when a unit is issued: lane l < R copies row l's
-  // codes, R <= l < 2R its scales, 2R <= l < 3R its zero-points.
-  const int role = lane / R;
-  const int rrow = lane % R;
-  // Unit (b, pass) of a window = rows [b*R, b*R+R) x groups [pass*32, pass*32+32).
-  auto issue = [&](int ub, int upass, int wg0, int wgn, int slot) {
-    const int gl0 = upass * 32;
-    const int ng = min(32, wgn - gl0);
-    const int nr = min(R, nrows - ub * R);
-    uint8_t* st = my_stages + slot * kStageBytes;
-    uint64_t* bar = my_bars + slot;
-    if (lane == 0) mbar_arrive_expect_tx(bar, uint32_t(nr * ng * (kGroupBytes + 2 + 1)));
-    __syncwarp();
-    if (role < 3 && rrow < nr) {
-      const int64_t row = r_begin + int64_t(ub) * R + rrow;
-      const int64_t g = int64_t(wg0 + gl0);
-      const void* src;
-      void* dst;
-      uint32_t bytes;
-      if (role == 0) {
-        src = p.packed + row * p.w_rs + g * kGroupBytes;
-        dst = st + rrow * 512;
-        bytes = uint32_t(ng * kGroupBytes);
-      } else if (role == 1) {
-        src = p.scales + row * p.s_rs + g;
-        dst = st + R * 512 + rrow * 64;
-        bytes = uint32_t(ng * 2);
+  // Weight registers: the batch being computed (c*) and the next one (n*).
+  uint4 nw[R];
+  float ns[R], nz[R];
+  auto load_batch = [&](int g, int row_rel) {  // g: absolute group; rows r_begin+row_rel..
+    const int64_t row0 = r_begin + row_rel;
+    const uint8_t* wp = p.packed + row0 * p.w_rs + int64_t(g) * kGroupBytes;
+    const __half* sp = p.scales + row0 * p.s_rs + int64_t(g) * p.s_cs;
+    const uint8_t* zp = p.zeros + row0 * p.z_rs + int64_t(g) * p.z_cs;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (row_rel + r < ge) {
+        nw[r] = load_group16<ALIGN>(wp + r * p.w_rs);
+        ns[r] = __half2float(__ldg(sp + r * p.s_rs));
+        nz[r] = __uint_as_float(uint32_t(__ldg(zp + r * p.z_rs)) | kMagic) - 8388608.0f;
       } else {
-        src = p.zeros + row * p.z_rs + g;
-        dst = st + R * 576 + rrow * 32;
-        bytes = uint32_t(ng);
+        nw[r] = make_uint4(0u, 0u, 0u, 0u);
+        ns[r] = 0.f;
+        nz[r] = 0.f;
       }
-      bulk_g2s(dst, src, bytes, bar);
     }
   };
-  // Units are dealt round-robin to the CTA's warps: v = warp, warp+8, ...
-  // with v = b*P + pass.  Advance (b, pass) by 8 units without dividing.
-  auto advance = [](int& ub, int& upass, int P) {
-    upass += kWarps;
-    while (upass >= P) { upass -= P; ++ub; }
-  };
 
-  const int nwin = (G + kp.win_groups - 1) / kp.win_groups;
-  uint32_t seq = 0;  // units consumed by this warp (stage = seq % nstages)
-
-  // Window-0 prologue before the dependency wait: weights are immutable.
-  int ib = 0, ip = 0;  // next unit to issue
+#pragma unroll
+  for (int r = 0; r < R; ++r) { nw[r] = make_uint4(0u, 0u, 0u, 0u); ns[r] = 0.f; nz[r] = 0.f; }
+  // First batch of window 0, before the dependency wait (weights only).
   {
-    const int wgn = min(kp.win_groups, G);
-    const int P = (wgn + 31) / 32;
-    ib = warp / P;
-    ip = warp % P;
-    for (int i = 0; i < nstages && ib < nb; ++i) {
-      issue(ib, ip, 0, wgn, i);
-      advance(ib, ip, P);
-    }
+    const int wgn0 = min(kp.win_groups, G);
+    const int gl = ks * 32 + lane;
+    if (gl < wgn0 && gb < ge) load_batch(gl, gb);
   }
 
   constexpr int kOutPerThread = 4;
@@ -548,54 +350,23 @@ __global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant
   uint32_t magic_reg;
   asm volatile("mov.b32 %0, 0x4B000000;" : "=r"(magic_reg));
 
+  const int nwin = (G + kp.win_groups - 1) / kp.win_groups;
   for (int w = 0; w < nwin; ++w) {
     const int wg0 = w * kp.win_groups;
     const int wgn = min(kp.win_groups, G - wg0);
-    const int P = (wgn + 31) / 32;
-    const int pass_base = w * ((kp.win_groups + 31) / 32);
-    if (w > 0) {
-      __syncthreads();  // every warp is done with the previous window's x
-      ib = warp / P;
-      ip = warp % P;
-      for (int i = 0; i < nstages && ib < nb; ++i) {
-        issue(ib, ip, wg0, wgn, int((seq + i) % nstages));
-        advance(ib, ip, P);
-      }
-    }
+    const int wpass = (wgn + 31) / 32;
+    const int pass_base = w * (kp.win_groups / 32);
+    if (w > 0) __syncthreads();  // every warp is done with the previous window's x
     stage_x_window(p, kp.vec_x, xs, xsum, wg0, wgn, tid, blockDim.x, lane);
     __syncthreads();
-    int cb = warp / P, cp = warp % P;  // unit being consumed
-    while (cb < nb) {
-      const uint32_t slot = seq % nstages;
-      uint64_t* bar = my_bars + slot;
-      if (!mbar_wait(bar, (seq / nstages) & 1u, &s_abort)) {
-        if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_timeouts, 1); }
-        break;
-      }
-      const uint8_t* st = my_stages + slot * kStageBytes;
-      const int gl = cp * 32 + lane;
-      const int nr = min(R, nrows - cb * R);
+    if (w > 0 && ks * 32 + lane < wgn && gb < ge) load_batch(wg0 + ks * 32 + lane, gb);
+
+    for (int pp = ks; pp < wpass; pp += S) {
+      const int gl = pp * 32 + lane;
       const bool lv = gl < wgn;
-      uint4 cw[R];
-      float cs[R], cz[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const bool ok = lv && r < nr;
-        cw[r] = ok ? *reinterpret_cast<const uint4*>(st + r * 512 + lane * 16) : make_uint4(0u, 0u, 0u, 0u);
-        cs[r] = ok ? __half2float(*reinterpret_cast<const __half*>(st + R * 512 + r * 64 + lane * 2)) : 0.f;
-        cz[r] = ok ? __uint_as_float(uint32_t(st[R * 576 + r * 32 + lane]) | kMagic) - 8388608.0f : 0.f;
-      }
-      // Refill this stage with the unit nstages ahead before computing.
-      if (ib < nb) {
-        fence_proxy_async_smem();
-        issue(ib, ip, wg0, wgn, int(slot));
-        advance(ib, ip, P);
-      }
-      float acc[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[r] = 0.f;
+      float2 xr[16];
+      float xg = 0.f;
       if (lv) {
-        float2 xr[16];
         const float4* src = reinterpret_cast<const float4*>(xs + gl * kXpStride);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -603,35 +374,47 @@ __global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant
           xr[2 * c] = make_float2(f.x, f.y);
           xr[2 * c + 1] = make_float2(f.z, f.w);
         }
-        const float xg = xsum[gl];
+        xg = xsum[gl];
+      }
+      for (int rb = gb; rb < ge; rb += R) {
+        uint4 cw[R];
+        float cs[R], cz[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) { cw[r] = nw[r]; cs[r] = ns[r]; cz[r] = nz[r]; }
+        // Keep the next batch in flight: next rows of this pass, else the
+        // first rows of this warp's next pass in the window.
+        if (rb + R < ge) {
+          if (lv) load_batch(wg0 + gl, rb + R);
+        } else if (pp + S < wpass) {
+          const int gn = (pp + S) * 32 + lane;
+          if (gn < wgn) load_batch(wg0 + gn, gb);
+        }
+        float acc[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          float q = group_qdot(cw[r], xr, magic_reg);
+          float q = lv ? group_qdot(cw[r], xr, magic_reg) : 0.f;
           q = fmaf(-cz[r], xg, q);
           acc[r] = q * cs[r];
         }
+        warp_transpose_reduce<R>(acc, lane);
+        constexpr int kLeaderMask = (32 / R) - 1;
+        const int rr = reduced_row<R>(lane);
+        if ((lane & kLeaderMask) == 0 && rb + rr < ge) red[(pass_base + pp) * kp.rows_max + rb + rr] = acc[0];
       }
-      warp_transpose_reduce<R>(acc, lane);
-      constexpr int kLeaderMask = (32 / R) - 1;
-      const int rr = reduced_row<R>(lane);
-      if ((lane & kLeaderMask) == 0 && rr < nr) red[(pass_base + cp) * kp.rows_max + cb * R + rr] = acc[0];
-      ++seq;
-      advance(cb, cp, P);
     }
   }
-  // Outlier columns: warp v takes rows 8v.., 8 rows per batch, read from the
-  // staged copy (or, when it could not be staged, straight from memory).
+
+  // Outlier columns (staged copy if available), 8 rows per warp batch.
   if (p.n_out > 0) {
     if (ow_staged) {
       if (!mbar_wait(&s_ow_bar, 0, &s_abort)) {
         if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_timeouts, 1); }
       } else {
-        // ragged tail (< 16 bytes) that the bulk copy left out
         for (int64_t bt = ow_a1 + tid; bt < ow_b1; bt += blockDim.x) ow_smem[bt - ow_a0] = ow_src[bt];
       }
     }
     __syncthreads();
-    for (int i0 = warp * 8; i0 < nrows; i0 += kWarps * 8) {
+    for (int i0 = warp * 8; i0 < nrows; i0 += nwarps * 8) {
       float oacc[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) oacc[r] = 0.f;
@@ -674,41 +457,47 @@ __global__ void __launch_bounds__(256, 1) gemv_bulk_kernel(const __grid_constant
 }
 
 template <int R, int ALIGN>
-int launch_r(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
-  auto kern = gemv_w4a16_kernel<R, ALIGN>;
+int launch_rows(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
+  auto kern = gemv_rows_kernel<R, ALIGN>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
-  // Per-device caches: opt-in shared-memory size and resident CTAs per SM.
-  static size_t set_bytes[kMaxDevices] = {};
-  static int occ_cache[kMaxDevices][4] = {};  // keyed by smem bucket
-  static int sms[kMaxDevices] = {};
   if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  if (pl.smem > 48 * 1024 && set_bytes[dev] < pl.smem) {
+  static bool attr_set[kMaxDevices] = {};
+  static int occ[kMaxDevices] = {};
+  if (!attr_set[dev]) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemvMaxSmem));
     if (e != cudaSuccess) return cuda_status(e);
-    set_bytes[dev] = kGemvMaxSmem;
+    attr_set[dev] = true;
   }
-  if (sms[dev] == 0) {
-    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return cuda_status(e);
+  const GemvArgs& a = kp.a;
+  auto r16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+  const int G = a.K / kGroup;
+  const int passes = kp.red_passes = (G + 31) / 32;
+  (void)passes;
+  const size_t xs_bytes = size_t(pl.win_groups) * kXpStride * 4 + r16(size_t(pl.win_groups) * 4) + r16(size_t(a.n_out) * 4);
+  // two CTAs per SM when the staged x leaves room, else one
+  const int per_sm = xs_bytes + 16 * 1024 <= 100 * 1024 ? 2 : 1;
+  const int64_t rows_group = int64_t(pl.RG) * R;
+  int64_t grid = std::min<int64_t>((a.N + rows_group - 1) / rows_group, int64_t(device_sms(dev)) * per_sm);
+  if (grid < 1) grid = 1;
+  kp.rows_max = int((a.N + grid - 1) / grid);
+  kp.off_xs = 0;
+  kp.off_xsum = int(size_t(pl.win_groups) * kXpStride * 4);
+  kp.off_xos = int(kp.off_xsum + r16(size_t(pl.win_groups) * 4));
+  kp.off_red = int(kp.off_xos + r16(size_t(a.n_out) * 4));
+  size_t smem = size_t(kp.off_red) + size_t(kp.red_passes + 1) * kp.rows_max * 4;
+  kp.off_ow = -1;
+  const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  if (a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && reinterpret_cast<uintptr_t>(a.ow) % 16 == 0) {
+    const size_t need = r16(size_t(kp.rows_max) * a.n_out * ow_es + 32);
+    if (r16(smem) + need <= (per_sm == 2 ? 110 * 1024 : kGemvMaxSmem)) {
+      kp.off_ow = int(r16(smem));
+      smem = r16(smem) + need;
+    }
   }
-  const int bucket = pl.smem <= 32 * 1024 ? 0 : pl.smem <= 64 * 1024 ? 1 : pl.smem <= 112 * 1024 ? 2 : 3;
-  const size_t bucket_bytes[4] = {32 * 1024, 64 * 1024, 112 * 1024, kGemvMaxSmem};
-  if (occ_cache[dev][bucket] == 0) {
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, bucket_bytes[bucket]);
-    if (e != cudaSuccess) return cuda_status(e);
-    occ_cache[dev][bucket] = occ < 1 ? 1 : occ;
-  }
-  const int64_t rows_cta = int64_t(pl.RG) * R;
-  const int64_t max_grid = int64_t(sms[dev]) * occ_cache[dev][bucket];
-  const int64_t want = (int64_t(kp.a.N) + rows_cta - 1) / rows_cta;
-  const int grid = int(want < max_grid ? want : max_grid);
-  // Multi-window K keeps per-row partial sums in shared memory across windows.
-  const int max_tiles = int(((int64_t(kp.a.N) + grid - 1) / grid + rows_cta - 1) / rows_cta);
-  size_t smem = pl.smem + (pl.win_groups < kp.a.K / kGroup ? size_t(max_tiles) * rows_cta * 4 : 0);
   if (smem > kGemvMaxSmem) return SPECTRA_ERR_UNSUPPORTED;
+  (void)occ;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
@@ -720,27 +509,339 @@ int launch_r(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, kp);
-  return cuda_status(e);
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, kp));
 }
 
-struct DevInfo {
-  int sms = 0;
-};
-inline int device_sms(int dev) {
-  static int sms[kMaxDevices] = {};
-  if (dev < 0 || dev >= kMaxDevices) return 148;
-  if (sms[dev] == 0) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-    sms[dev] = v;
+template <int ALIGN>
+int launch_rows_align(const GemvKParams& kp, const GemvPlan& pl, cudaStream_t st) {
+  switch (pl.R) {
+    case 4: return launch_rows<4, ALIGN>(kp, pl, st);
+    case 2: return launch_rows<2, ALIGN>(kp, pl, st);
+    default: return launch_rows<1, ALIGN>(kp, pl, st);
   }
-  return sms[dev];
 }
 
-template <int R>
-int launch_bulk(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
-  auto kern = gemv_bulk_kernel<R>;
+// ---------------------------------------------------------------------------
+// Tensor-core kernel (main path for bf16 / fp16 activations).
+//
+// The dot products run on mma.sync.m16n8k16 with fp32 accumulation:
+//   A (16 x 16): codes of 16 weight rows, as 16-bit pairs OFF+q built with one
+//                LOP3 (plus a shift) per pair -- exact small integers;
+//   B (16 x 8):  block-diagonal x -- column n carries x only in the k-slots
+//                that belong to quantisation group n of an 8-group block, so
+//                after the 16 MMAs of a block D[row][n] is group n's dot;
+//   thread (g, c) loads the codes of groups 2c and 2c+1 of rows g and g+8 and
+//   ends up holding exactly their four dots, to which it applies the group's
+//   scale and zero point in fp32:  s * (D - (OFF + z) * X_g),  X_g = sum of x.
+// A unit of work is 16 rows x 8 groups (4096 codes); a CTA's units are dealt
+// round-robin to its warps and each unit's partial row sums go to shared
+// memory, summed in a fixed order at the end (deterministic).
+// ---------------------------------------------------------------------------
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// Pair type t of a 32-bit code word (bytes b0..b3): t=0 {b0.lo, b2.lo},
+// t=1 {b0.hi, b2.hi}, t=2 {b1.lo, b3.lo}, t=3 {b1.hi, b3.hi}.  One shift
+// brings the pair's nibbles to the top four mantissa bits of each 16-bit
+// half, one LOP3 masks them and ORs in the exponent of 16.0: each half is
+// then exactly 16 + q (bf16: nibble at bits 3-6; fp16: bits 6-9).  The small
+// offset keeps the fp32 accumulation of (16 + q) * x as accurate as q * x.
+template <bool BF16, int T>
+__device__ __forceinline__ uint32_t pair_code(uint32_t w, uint32_t magic_reg) {
+  constexpr int kShift = BF16 ? 3 - 4 * T : 6 - 4 * T;  // > 0: left shift
+  constexpr uint32_t kMask = BF16 ? 0x00780078u : 0x03C003C0u;
+  const uint32_t v = kShift >= 0 ? (w << (kShift >= 0 ? kShift : 0)) : (w >> (kShift < 0 ? -kShift : 0));
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "n"(kMask), "r"(magic_reg));
+  return r;
+}
+
+// k (0..31, within the group) of the low / high code of pair kk = 4j + t.
+__host__ __device__ __forceinline__ int pair_k(int kk, int high, int layout) {
+  const int j = kk >> 2, t = kk & 3;
+  const int byte = 4 * j + 2 * high + (t >> 1);
+  return code_k(byte, t & 1, layout);
+}
+
+struct MmaUnitRegs {
+  uint4 w[4];     // codes: [grpA row g, grpA row g+8, grpB row g, grpB row g+8]
+  uint32_t s[2];  // scales (fp16 pairs {grpA, grpB}) of rows g, g+8
+  uint32_t z[2];  // zero points (byte pairs {grpA, grpB}) of rows g, g+8
+};
+
+template <bool BF16, int ALIGN>
+__global__ void __launch_bounds__(256, 2) gemv_mma_kernel(const __grid_constant__ GemvKParams kp) {
+  using namespace sm100;
+  const GemvArgs& p = kp.a;
+  constexpr uint32_t kMagic2 = BF16 ? 0x41804180u : 0x4C004C00u;  // 16.0 in both halves
+  constexpr float kOff = 16.0f;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint32_t* xp = reinterpret_cast<uint32_t*>(smem_raw + kp.off_xs);  // [win_groups + 1][16] pairs (+ zero pad)
+  float* xsum = reinterpret_cast<float*>(smem_raw + kp.off_xsum);     // [win_groups]
+  float* xos = reinterpret_cast<float*>(smem_raw + kp.off_xos);
+  float* red = reinterpret_cast<float*>(smem_raw + kp.off_red);       // [G/8 blocks][rows_max]
+  float* ored = red + kp.red_passes * kp.rows_max;                    // [rows_max]
+  __shared__ int s_abort;
+  __shared__ __align__(8) uint64_t s_ow_bar;
+
+  griddep_launch_dependents();
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  // 16-row blocks are dealt to CTAs evenly; only the matrix's last block is ragged.
+  const int64_t nblk = (int64_t(p.N) + 15) / 16;
+  const int64_t b0 = (nblk * blockIdx.x) / gridDim.x;
+  const int64_t b1 = (nblk * (blockIdx.x + 1)) / gridDim.x;
+  const int nrb = int(b1 - b0);
+  const int64_t r_begin = b0 * 16;
+  const int64_t r_end = (int64_t(p.N) < b1 * 16) ? int64_t(p.N) : b1 * 16;
+  const int nrows = int(r_end - r_begin);
+  const int G = p.K / kGroup;
+
+  if (tid == 0) s_abort = 0;
+  for (int i = tid; i < (kp.red_passes + 1) * kp.rows_max; i += blockDim.x) red[i] = 0.f;
+
+  const int ow_es = p.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  const bool ow_staged = kp.off_ow >= 0 && p.n_out > 0;
+  const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
+  const int64_t ow_b0 = r_begin * p.n_out * ow_es;
+  const int64_t ow_b1 = r_end * p.n_out * ow_es;
+  const int64_t ow_a0 = ow_b0 & ~int64_t(15);
+  const int64_t ow_a1 = ow_b1 & ~int64_t(15);
+  uint8_t* ow_smem = smem_raw + (kp.off_ow >= 0 ? kp.off_ow : 0);
+  if (ow_staged && tid == 0) {
+    mbar_init(&s_ow_bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&s_ow_bar, uint32_t(ow_a1 - ow_a0));
+    if (ow_a1 > ow_a0) bulk_g2s(ow_smem, ow_src + ow_a0, uint32_t(ow_a1 - ow_a0), &s_ow_bar);
+  }
+
+  // Load unit (rbi, kb): rows r_begin + 16*rbi + {g, g+8}, groups 8*kb + {2c, 2c+1} of the window.
+  auto load_unit = [&](MmaUnitRegs& u, int rbi, int kb, int wg0, int wgn) {
+    const int gA = kb * 8 + 2 * c;
+    const bool va = gA < wgn, vb = gA + 1 < wgn;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t row = r_begin + rbi * 16 + g + 8 * h;
+      const bool vr = row < r_end;
+      const int64_t gabs = int64_t(wg0 + gA);
+      const uint8_t* wp = p.packed + row * p.w_rs + gabs * kGroupBytes;
+      u.w[h] = (vr && va) ? load_group16<ALIGN>(wp) : make_uint4(0u, 0u, 0u, 0u);
+      u.w[2 + h] = (vr && vb) ? load_group16<ALIGN>(wp + kGroupBytes) : make_uint4(0u, 0u, 0u, 0u);
+      const uint16_t* sp = reinterpret_cast<const uint16_t*>(p.scales) + row * p.s_rs + gabs * p.s_cs;
+      const uint8_t* zp = p.zeros + row * p.z_rs + gabs * p.z_cs;
+      const uint32_t sa = (vr && va) ? uint32_t(__ldg(sp)) : 0u;
+      const uint32_t sb = (vr && vb) ? uint32_t(__ldg(sp + p.s_cs)) : 0u;
+      const uint32_t za = (vr && va) ? uint32_t(__ldg(zp)) : 0u;
+      const uint32_t zb = (vr && vb) ? uint32_t(__ldg(zp + p.z_cs)) : 0u;
+      u.s[h] = sa | (sb << 16);
+      u.z[h] = za | (zb << 16);
+    }
+  };
+
+  constexpr int kOutPerThread = 4;
+  int64_t oidx[kOutPerThread];
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m) {
+    const int j = tid + m * blockDim.x;
+    oidx[m] = (j < p.n_out) ? load_index(p.idx, j, p.idx_dtype) : -1;
+  }
+
+  const int nwin = (G + kp.win_groups - 1) / kp.win_groups;
+  MmaUnitRegs nxt;
+  // first unit of window 0 before the dependency wait (weights only)
+  int cb = 0, ck = 0;  // unit being consumed: row-block cb, 8-group block ck
+  {
+    const int wgn = min(kp.win_groups, G);
+    const int KB = (wgn + 7) / 8;
+    cb = warp / KB;
+    ck = warp % KB;
+    if (cb < nrb) load_unit(nxt, cb, ck, 0, wgn);
+  }
+
+  griddep_wait();
+
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m) {
+    const int j = tid + m * blockDim.x;
+    if (j < p.n_out) xos[j] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_as_float(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0.f;
+  }
+  for (int j = tid + kOutPerThread * blockDim.x; j < p.n_out; j += blockDim.x) {
+    const int64_t k = load_index(p.idx, j, p.idx_dtype);
+    xos[j] = (k >= 0 && k < p.K) ? load_as_float(p.x, k * p.x_stride, p.x_dtype) : 0.f;
+  }
+
+  uint32_t magic_reg;
+  asm volatile("mov.b32 %0, %1;" : "=r"(magic_reg) : "n"(kMagic2));
+  const uint16_t* xh = reinterpret_cast<const uint16_t*>(p.x);
+
+  for (int w = 0; w < nwin; ++w) {
+    const int wg0 = w * kp.win_groups;
+    const int wgn = min(kp.win_groups, G - wg0);
+    const int KB = (wgn + 7) / 8;
+    const int kb_base = w * (kp.win_groups / 8);
+    if (w > 0) {
+      __syncthreads();  // every warp is done with the previous window's x
+      cb = warp / KB;
+      ck = warp % KB;
+      if (cb < nrb) load_unit(nxt, cb, ck, wg0, wgn);
+    }
+    // Stage x as 16 pairs per group in MMA order (x in the MMA's dtype is
+    // copied bit-exactly) and the per-group sums X_g, plus a zero pad group.
+    const int nstage = (wgn + 1) * 16;
+    for (int e0 = tid - lane; e0 < nstage; e0 += blockDim.x) {  // warp-uniform trip count
+      const int e = e0 + lane;
+      const int gl = e >> 4, kk = e & 15;
+      uint32_t v = 0u;
+      float sum2 = 0.f;
+      if (gl < wgn) {
+        const int64_t kbase = int64_t(wg0 + gl) * kGroup;
+        const int64_t klo = kbase + pair_k(kk, 0, p.layout), khi = kbase + pair_k(kk, 1, p.layout);
+        const uint32_t lo = __ldg(xh + klo * p.x_stride), hi = __ldg(xh + khi * p.x_stride);
+        v = lo | (hi << 16);
+        sum2 = BF16 ? (__uint_as_float(lo << 16) + __uint_as_float(hi << 16))
+                    : (__half2float(__ushort_as_half(uint16_t(lo))) + __half2float(__ushort_as_half(uint16_t(hi))));
+      }
+      if (e < nstage) xp[e] = v;
+      // 16 consecutive lanes hold one group's pairs
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
+      if ((lane & 15) == 0 && gl < wgn) xsum[gl] = sum2;
+    }
+    __syncthreads();
+
+    const uint32_t* xzero = xp + wgn * 16;
+    const bool lane_a = (lane % 9) == 0;        // lanes 0, 9, 18, 27: B column 2c
+    const bool lane_b = (lane % 9) == 4;        // lanes 4, 13, 22, 31: B column 2c+1
+    while (cb < nrb) {
+      MmaUnitRegs cur = nxt;
+      const int rbi = cb, kbi = ck;
+      // next unit of this warp: 8-group block ck + nwarps (row-block advances)
+      ck += nwarps;
+      while (ck >= KB) { ck -= KB; ++cb; }
+      if (cb < nrb) load_unit(nxt, cb, ck, wg0, wgn);
+
+      const int gA = kbi * 8 + 2 * c;  // this thread's groups (window-relative)
+      // B fragments: x pairs of group gA (lane_a) or gA+1 (lane_b), else zero
+      const uint4* srcA = reinterpret_cast<const uint4*>(lane_a && gA < wgn ? xp + gA * 16 : xzero);
+      const uint4* srcB = reinterpret_cast<const uint4*>(lane_b && gA + 1 < wgn ? xp + (gA + 1) * 16 : xzero);
+      uint32_t bA[16], bB[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 ta = srcA[q], tb = srcB[q];
+        bA[4 * q] = ta.x; bA[4 * q + 1] = ta.y; bA[4 * q + 2] = ta.z; bA[4 * q + 3] = ta.w;
+        bB[4 * q] = tb.x; bB[4 * q + 1] = tb.y; bB[4 * q + 2] = tb.z; bB[4 * q + 3] = tb.w;
+      }
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t wa[4][4] = {{cur.w[0].x, cur.w[0].y, cur.w[0].z, cur.w[0].w},
+                                 {cur.w[1].x, cur.w[1].y, cur.w[1].z, cur.w[1].w},
+                                 {cur.w[2].x, cur.w[2].y, cur.w[2].z, cur.w[2].w},
+                                 {cur.w[3].x, cur.w[3].y, cur.w[3].z, cur.w[3].w}};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#define SPECTRA_MMA_STEP(T)                                                                                   \
+  mma16816<BF16>(d, pair_code<BF16, T>(wa[0][j], magic_reg), pair_code<BF16, T>(wa[1][j], magic_reg),           \
+                 pair_code<BF16, T>(wa[2][j], magic_reg), pair_code<BF16, T>(wa[3][j], magic_reg),              \
+                 bA[4 * j + T], bB[4 * j + T]);
+        SPECTRA_MMA_STEP(0) SPECTRA_MMA_STEP(1) SPECTRA_MMA_STEP(2) SPECTRA_MMA_STEP(3)
+#undef SPECTRA_MMA_STEP
+      }
+      // d = {D[g][gA], D[g][gA+1], D[g+8][gA], D[g+8][gA+1]}
+      const float XA = (gA < wgn) ? xsum[gA] : 0.f;
+      const float XB = (gA + 1 < wgn) ? xsum[gA + 1] : 0.f;
+      float rs[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float sa = __half2float(__ushort_as_half(uint16_t(cur.s[h] & 0xFFFFu)));
+        const float sb = __half2float(__ushort_as_half(uint16_t(cur.s[h] >> 16)));
+        const float za = __uint_as_float((cur.z[h] & 0xFFu) | kMagic) - 8388608.0f + kOff;
+        const float zb = __uint_as_float(((cur.z[h] >> 16) & 0xFFu) | kMagic) - 8388608.0f + kOff;
+        rs[h] = sa * fmaf(-za, XA, d[2 * h]) + sb * fmaf(-zb, XB, d[2 * h + 1]);
+      }
+      // sum the 4 threads of a quad: rows g and g+8 over this unit's 8 groups
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+        rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      }
+      if (c == 0) {
+        float* rr = red + (kb_base + kbi) * kp.rows_max + rbi * 16 + g;
+        if (rbi * 16 + g < nrows) rr[0] = rs[0];
+        if (rbi * 16 + g + 8 < nrows) rr[8] = rs[1];
+      }
+    }
+  }
+
+  // Outlier columns (staged copy if available), 8 rows per warp batch.
+  if (p.n_out > 0) {
+    if (ow_staged) {
+      if (!mbar_wait(&s_ow_bar, 0, &s_abort)) {
+        if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_timeouts, 1); }
+      } else {
+        for (int64_t bt = ow_a1 + tid; bt < ow_b1; bt += blockDim.x) ow_smem[bt - ow_a0] = ow_src[bt];
+      }
+    }
+    __syncthreads();
+    const bool ow_bf16 = p.ow_dtype == SPECTRA_DT_BF16;
+    for (int i0 = warp * 8; i0 < nrows; i0 += nwarps * 8) {
+      float oacc[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) oacc[r] = 0.f;
+      for (int j0 = 0; j0 < p.n_out; j0 += 32) {
+        const int j = j0 + lane;
+        float ov[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          ov[r] = 0.f;
+          if (j < p.n_out && i0 + r < nrows) {
+            if (ow_staged) {
+              const uint8_t* q = ow_smem + (int64_t(i0 + r) * p.n_out + j) * ow_es + (ow_b0 - ow_a0);
+              ov[r] = ow_es == 4 ? *reinterpret_cast<const float*>(q)
+                      : ow_bf16 ? __uint_as_float(uint32_t(*reinterpret_cast<const uint16_t*>(q)) << 16)
+                                : __half2float(*reinterpret_cast<const __half*>(q));
+            } else {
+              ov[r] = load_as_float(p.ow, (r_begin + i0 + r) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype);
+            }
+          }
+        }
+        const float xo = j < p.n_out ? xos[j] : 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) oacc[r] = fmaf(xo, ov[r], oacc[r]);
+      }
+      warp_transpose_reduce<8>(oacc, lane);
+      const int rr = reduced_row<8>(lane);
+      if ((lane & 3) == 0 && i0 + rr < nrows) ored[i0 + rr] = oacc[0];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < nrows; i += blockDim.x) {
+    const int64_t row = r_begin + i;
+    float v = ored[i];
+    for (int q = 0; q < kp.red_passes; ++q) v += red[q * kp.rows_max + i];
+    if (p.bias) v += load_as_float(p.bias, row, p.bias_dtype);
+    store_from_float(p.y, row * p.y_stride, p.y_dtype, v);
+  }
+}
+
+template <bool BF16, int ALIGN>
+int launch_mma(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
+  auto kern = gemv_mma_kernel<BF16, ALIGN>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -752,43 +853,32 @@ int launch_bulk(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const GemvArgs& a = kp.a;
-  constexpr int kWarps = 8;
-  const int stage_bytes = R * (512 + 64 + 32);
   auto r16 = [](size_t v) { return (v + 15) & ~size_t(15); };
   const int G = a.K / kGroup;
-  const int passes = (G + 31) / 32;
-  int64_t grid = std::min<int64_t>((a.N + R - 1) / R, device_sms(dev));
+  kp.red_passes = (G + 7) / 8;  // partial-sum slots: one per 8-group block of K
+  const int64_t nblk = (int64_t(a.N) + 15) / 16;
+  int64_t grid = std::min<int64_t>(nblk, int64_t(device_sms(dev)) * 2);
   if (grid < 1) grid = 1;
-  kp.rows_max = int((a.N + grid - 1) / grid);
-  kp.red_passes = passes;
-  const size_t tail = size_t(pl.win_groups) * kXpStride * 4 + r16(size_t(pl.win_groups) * 4) + r16(size_t(a.n_out) * 4) +
-                      size_t(passes + 1) * kp.rows_max * 4;
-  // Deepest ring (<= 4 stages per warp) that fits next to the staged x.
-  int nst = 4;
-  while (nst > 2 && size_t(kWarps) * nst * stage_bytes + r16(size_t(kWarps) * nst * 8) + tail > kGemvMaxSmem) --nst;
-  kp.S = nst;
-  kp.off_bars = kWarps * nst * stage_bytes;
-  kp.off_xs = int(kp.off_bars + r16(size_t(kWarps) * nst * 8));
-  kp.off_xsum = int(kp.off_xs + size_t(pl.win_groups) * kXpStride * 4);
+  kp.rows_max = int(((nblk + grid - 1) / grid) * 16);
+  kp.off_xs = 0;
+  kp.off_xsum = int(r16(size_t(pl.win_groups + 1) * 64));
   kp.off_xos = int(kp.off_xsum + r16(size_t(pl.win_groups) * 4));
   kp.off_red = int(kp.off_xos + r16(size_t(a.n_out) * 4));
-  size_t smem = size_t(kp.off_red) + size_t(passes + 1) * kp.rows_max * 4;
-  if (smem > kGemvMaxSmem) return SPECTRA_ERR_UNSUPPORTED;
-  // Stage the outlier weights when they are one contiguous, 16-byte aligned
-  // row-major block and the CTA's share fits (plus 32 bytes of alignment slack).
+  size_t smem = size_t(kp.off_red) + size_t(kp.red_passes + 1) * kp.rows_max * 4;
   kp.off_ow = -1;
   const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   if (a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && reinterpret_cast<uintptr_t>(a.ow) % 16 == 0) {
     const size_t need = r16(size_t(kp.rows_max) * a.n_out * ow_es + 32);
-    if (r16(smem) + need <= kGemvMaxSmem) {
+    if (r16(smem) + need <= 110 * 1024) {
       kp.off_ow = int(r16(smem));
       smem = r16(smem) + need;
     }
   }
+  if (smem > kGemvMaxSmem) return SPECTRA_ERR_UNSUPPORTED;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(kWarps * 32);
+  cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -797,26 +887,6 @@ int launch_bulk(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, kp));
-}
-
-// The bulk path needs 16-byte aligned row segments of packed codes, scales
-// and zeros (cp.async.bulk sizes and addresses are multiples of 16).
-bool bulk_eligible(const GemvArgs& a) {
-  const uintptr_t wp = reinterpret_cast<uintptr_t>(a.packed);
-  const uintptr_t sp = reinterpret_cast<uintptr_t>(a.scales);
-  const uintptr_t zp = reinterpret_cast<uintptr_t>(a.zeros);
-  const int G = a.K / kGroup;
-  return (G % 16) == 0 && wp % 16 == 0 && a.w_rs % 16 == 0 && sp % 16 == 0 && a.s_cs == 1 && a.s_rs % 8 == 0 &&
-         zp % 16 == 0 && a.z_cs == 1 && a.z_rs % 16 == 0 && a.w_rs >= 0 && a.s_rs >= 0 && a.z_rs >= 0;
-}
-
-template <int ALIGN>
-int launch_align(const GemvKParams& kp, const GemvPlan& pl, cudaStream_t st) {
-  switch (pl.R) {
-    case 4: return launch_r<4, ALIGN>(kp, pl, st);
-    case 2: return launch_r<2, ALIGN>(kp, pl, st);
-    default: return launch_r<1, ALIGN>(kp, pl, st);
-  }
 }
 
 }  // namespace
@@ -856,12 +926,19 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   kp.smem_xs_floats = pl.win_groups * kXpStride;
   kp.vec_x = a.x_stride == 1 && (reinterpret_cast<uintptr_t>(a.x) % 16) == 0 &&
              (a.x_dtype == SPECTRA_DT_BF16 || a.x_dtype == SPECTRA_DT_F16);
-  if (bulk_eligible(a) && bulk_path_enabled()) return launch_bulk<8>(kp, pl, st);
   const uintptr_t base = reinterpret_cast<uintptr_t>(a.packed);
   const int align = ((base | uintptr_t(a.w_rs)) % 16 == 0) ? 16 : (((base | uintptr_t(a.w_rs)) % 4 == 0) ? 4 : 1);
-  if (align == 16) return launch_align<16>(kp, pl, st);
-  if (align == 4) return launch_align<4>(kp, pl, st);
-  return launch_align<1>(kp, pl, st);
+  // bf16 / fp16 activations: tensor-core kernel; fp32 activations keep the
+  // exact CUDA-core kernel (an fp32 x cannot be an MMA operand unrounded).
+  if (mma_path_enabled() && (a.x_dtype == SPECTRA_DT_BF16 || a.x_dtype == SPECTRA_DT_F16)) {
+    const bool bf = a.x_dtype == SPECTRA_DT_BF16;
+    if (align == 16) return bf ? launch_mma<true, 16>(kp, pl, st) : launch_mma<false, 16>(kp, pl, st);
+    if (align == 4) return bf ? launch_mma<true, 4>(kp, pl, st) : launch_mma<false, 4>(kp, pl, st);
+    return bf ? launch_mma<true, 1>(kp, pl, st) : launch_mma<false, 1>(kp, pl, st);
+  }
+  if (align == 16) return launch_rows_align<16>(kp, pl, st);
+  if (align == 4) return launch_rows_align<4>(kp, pl, st);
+  return launch_rows_align<1>(kp, pl, st);
 }
 
 }  // namespace spectra

@@ -79,7 +79,9 @@ def test_gemv_matches_reference_triton_outputs(golden_dir, name, dt, marlin, use
     y_ref = (O.bf16_bits_to_f32(yb) if dt == "bf16" else yb.view(np.float16)).astype(np.float64).reshape(-1)
     got = out_f64(y).reshape(-1)
     # the reference's own Triton result and ours: both round an fp32 sum once
-    assert np.all(np.abs(got - y_ref) <= ulp(y_ref, dt)), name
+    d_ulp = np.abs(got - y_ref) / ulp(y_ref, dt)
+    i = int(np.argmax(d_ulp))
+    assert d_ulp[i] <= 1.0, f"{name}: worst at {i}: got {got[i]!r} ref {y_ref[i]!r} ({d_ulp[i]:.2f} ulp)"
     if dt == "f16":
         assert np.max(np.abs(got - y_ref)) <= 0.05  # tests/test_kernels.py:49
     y_exact, y_round, od = oracle_gemv(fmt, x, marlin, bias, use_out)
