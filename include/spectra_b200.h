@@ -114,6 +114,37 @@ SPECTRA_API int spectra_w4a16_dequant(
     void* out, int out_dtype, int64_t out_row_stride,
     int64_t N, int64_t K, int layout, void* stream);
 
+/*
+ * M >= 2 GEMM on the tensor cores.
+ * Replaces spectra/kernels.py:333-389 (batched_w4a16_gemm, the wrapper) and
+ * spectra/kernels.py:191-331 (_batched_w4a16_gemm_kernel).
+ *   c[m,n] = sum_k a[m,k] * R((q-z)*s) + sum_j a[m,idx_j] * R(ow[n,j])
+ * where R() rounds to a's dtype (the reference's tensor-core operands),
+ * accumulated in fp32 and rounded once to c (same dtype as a).  No bias
+ * (the engine adds it, spectra/engine.py:122-123).
+ *   a      [M, K] at a + m*a_row_stride + k; a_dtype F16|BF16; 16-byte aligned
+ *          base, row stride a multiple of 8 elements (TMA tensor map)
+ *   packed row n at packed + n*w_row_stride; base and row stride 16-byte aligned
+ *   c      [M, N] at c + m*c_row_stride + n, c_dtype == a_dtype
+ *   workspace: caller-owned device memory of at least
+ *          spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out) bytes, zeroed once
+ *          before its first use; every call leaves its counter region zero
+ *          again.  Calls that share a workspace must not overlap in time.
+ */
+SPECTRA_API int spectra_w4a16_gemm(
+    const void* a, int a_dtype, int64_t a_row_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* c, int c_dtype, int64_t c_row_stride,
+    int64_t M, int64_t N, int64_t K, int layout,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes spectra_w4a16_gemm needs for this problem (0: none). */
+SPECTRA_API size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -5,6 +5,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "gemm.h"
 #include "gemv.h"
 
 namespace spectra {
@@ -128,6 +129,51 @@ int spectra_w4a16_dequant(
   a.out = out; a.out_dtype = out_dtype; a.out_rs = out_row_stride;
   a.N = N; a.K = int(K); a.layout = layout;
   return launch_dequant(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_w4a16_gemm(
+    const void* a, int a_dtype, int64_t a_row_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* c, int c_dtype, int64_t c_row_stride,
+    int64_t M, int64_t N, int64_t K, int layout,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_weights(packed, scales, zeros, N, K, layout);
+  if (st != SPECTRA_OK) return st;
+  if (!a || !c) return SPECTRA_ERR_NULL_POINTER;
+  if (M <= 0 || !fits_i32(M) || int64_t(M) * N > INT32_MAX) return SPECTRA_ERR_SHAPE;
+  if (a_dtype != SPECTRA_DT_F16 && a_dtype != SPECTRA_DT_BF16) return SPECTRA_ERR_DTYPE;
+  if (c_dtype != a_dtype) return SPECTRA_ERR_DTYPE;
+  if (n_out < 0 || !fits_i32(n_out)) return SPECTRA_ERR_SHAPE;
+  const bool has_out = n_out > 0;
+  if (has_out && (!outlier_idx || !outlier_w)) return SPECTRA_ERR_NULL_POINTER;
+  if (has_out && (!is_index_dt(idx_dtype) || !is_float_dt(ow_dtype))) return SPECTRA_ERR_DTYPE;
+  // tensor-map requirements (16-byte aligned bases and row strides)
+  if (reinterpret_cast<uintptr_t>(a) % 16 != 0 || (a_row_stride * 2) % 16 != 0 || a_row_stride < K)
+    return SPECTRA_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(packed) % 16 != 0 || w_row_stride % 16 != 0 || w_row_stride < K / 2)
+    return SPECTRA_ERR_ALIGNMENT;
+  if (!aligned(c, 2) || (c_row_stride < N && M > 1)) return SPECTRA_ERR_STRIDE;
+  if (has_out && (!aligned(outlier_idx, dt_size(idx_dtype)) || !aligned(outlier_w, dt_size(ow_dtype))))
+    return SPECTRA_ERR_ALIGNMENT;
+  GemmArgs g;
+  g.a = a; g.a_dtype = a_dtype; g.a_rs = a_row_stride;
+  g.packed = packed; g.w_rs = w_row_stride;
+  g.scales = reinterpret_cast<const __half*>(scales); g.s_rs = s_row_stride; g.s_cs = s_col_stride;
+  g.zeros = zeros; g.z_rs = z_row_stride; g.z_cs = z_col_stride;
+  g.idx = has_out ? outlier_idx : nullptr; g.idx_dtype = idx_dtype; g.n_out = has_out ? int(n_out) : 0;
+  g.ow = has_out ? outlier_w : nullptr; g.ow_dtype = ow_dtype; g.ow_rs = ow_row_stride; g.ow_cs = ow_col_stride;
+  g.c = c; g.c_dtype = c_dtype; g.c_rs = c_row_stride;
+  g.M = int(M); g.N = int(N); g.K = int(K); g.layout = layout;
+  return launch_gemm(g, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return plan_gemm(M, N, K, n_out).workspace;
 }
 
 }  // extern "C"

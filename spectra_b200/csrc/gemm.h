@@ -1,0 +1,33 @@
+// Internal interface of the tensor-core GEMM launcher (not part of the public C ABI).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace spectra {
+
+struct GemmArgs {
+  const void* a; int a_dtype; int64_t a_rs;           // [M, K], unit column stride
+  const uint8_t* packed; int64_t w_rs;
+  const __half* scales; int64_t s_rs, s_cs;
+  const uint8_t* zeros; int64_t z_rs, z_cs;
+  const void* idx; int idx_dtype; int n_out;
+  const void* ow; int ow_dtype; int64_t ow_rs, ow_cs;
+  void* c; int c_dtype; int64_t c_rs;                 // [M, N], unit column stride, a's dtype
+  int M, N, K, layout;
+};
+
+struct GemmPlan {
+  int MT, m_chunks, tiles_n, nk, n_os, S, stages, act_stage_bytes;
+  uint32_t tmem_cols;
+  size_t smem, workspace;
+};
+
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out);
+int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st);
+
+}  // namespace spectra

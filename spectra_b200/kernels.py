@@ -138,6 +138,82 @@ def fused_w4a16_gemv_hdsq(
     return out
 
 
+# Split-K workspace, one per (device, stream): calls that share one must not
+# overlap in time, and calls on one stream never do.  Zeroed when allocated;
+# every GEMM call leaves its counters zero again.
+_WORKSPACES: dict = {}
+
+
+def _workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (dev.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def batched_w4a16_gemm(
+    a: torch.Tensor,
+    packed_b: torch.Tensor,
+    scales: torch.Tensor,
+    zeros: torch.Tensor,
+    outlier_idx: Optional[torch.Tensor] = None,
+    outlier_w: Optional[torch.Tensor] = None,
+    marlin_layout: bool = False,
+) -> torch.Tensor:
+    """M >= 2 W4A16 GEMM on the tcgen05 tensor cores (spectra/kernels.py:333-389).
+
+    ``a`` is [..., K]; the result is [..., N] in a's dtype.  Operands are rounded
+    to the compute dtype (bf16 if ``a`` is bf16, else fp16) exactly as the
+    reference does; fp32 ``a`` is rounded to fp16 before the call, the same
+    rounding the reference applies when it loads it.  No bias is added.
+    """
+    orig_shape = a.shape
+    K = a.shape[-1]
+    M = a.numel() // K if K else 0
+    N = packed_b.shape[0]
+    dev = a.device
+    for name, t in (("packed_b", packed_b), ("scales", scales), ("zeros", zeros),
+                    ("outlier_idx", outlier_idx), ("outlier_w", outlier_w)):
+        _require_cuda(name, t, dev)
+    _require_cuda("a", a, dev)
+    packed, scales, zeros = _weights(packed_b, scales, zeros)
+    idx, ow, n_out = _outliers(outlier_idx, outlier_w, N)
+    compute = torch.bfloat16 if a.dtype == torch.bfloat16 else torch.float16
+    c = torch.empty((M, N), device=dev, dtype=compute)
+    if M == 0 or N == 0:
+        return c.reshape(orig_shape[:-1] + (N,)).to(a.dtype)
+    a2 = a.reshape(M, K)
+    if a2.dtype != compute:
+        a2 = a2.to(compute)
+    # the activation tile is fetched by TMA: unit column stride, 16-byte
+    # aligned base and row pitch
+    if a2.stride(1) != 1 or (a2.stride(0) * 2) % 16 or a2.data_ptr() % 16 or a2.stride(0) < K:
+        a2 = a2.clone(memory_format=torch.contiguous_format)
+    if packed.data_ptr() % 16 or packed.stride(0) % 16:
+        packed = packed.clone(memory_format=torch.contiguous_format)
+    layout = L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD
+    lib = L.lib()
+    with torch.cuda.device(dev):
+        stream = _stream(dev)
+        nbytes = lib.spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out)
+        ws = _workspace(dev, stream, nbytes) if nbytes else None
+        st = lib.spectra_w4a16_gemm(
+            a2.data_ptr(), _dt(a2), a2.stride(0),
+            packed.data_ptr(), packed.stride(0),
+            scales.data_ptr(), scales.stride(0), scales.stride(1),
+            zeros.data_ptr(), zeros.stride(0), zeros.stride(1),
+            idx.data_ptr() if idx is not None else None, _dt(idx) if idx is not None else 0, n_out,
+            ow.data_ptr() if ow is not None else None, _dt(ow) if ow is not None else 0,
+            ow.stride(0) if ow is not None else 0, ow.stride(1) if ow is not None else 0,
+            c.data_ptr(), _dt(c), c.stride(0),
+            M, N, K, layout,
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
+    L.check("spectra_w4a16_gemm", st)
+    return c.reshape(orig_shape[:-1] + (N,)).to(a.dtype)
+
+
 def dequantize(packed_w: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                marlin_layout: bool = False, dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Dense ``(q - z) * s`` on the GPU: exact in fp32, or rounded to nearest-even

@@ -97,6 +97,50 @@ def test_dequant_rejects_bad_arguments_on_host():
     assert f(*{**ok, "out": P + 2}.values()) == L.ERR_ALIGNMENT
 
 
+def _gemm(**kw):
+    args = dict(a=P, a_dtype=L.DT_BF16, a_rs=128, packed=P, w_rs=64, scales=P, s_rs=4, s_cs=1,
+                zeros=P, z_rs=4, z_cs=1, idx=None, idx_dtype=0, n_out=0,
+                ow=None, ow_dtype=0, ow_rs=0, ow_cs=0, c=P, c_dtype=L.DT_BF16, c_rs=4096,
+                M=16, N=4096, K=128, layout=L.LAYOUT_MARLIN, ws=None, ws_bytes=0, stream=None)
+    args.update(kw)
+    return L.lib().spectra_w4a16_gemm(*args.values())
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(K=48), L.ERR_SHAPE),
+    (dict(M=0), L.ERR_SHAPE),
+    (dict(M=-3), L.ERR_SHAPE),
+    (dict(a=None), L.ERR_NULL_POINTER),
+    (dict(c=None), L.ERR_NULL_POINTER),
+    (dict(n_out=3), L.ERR_NULL_POINTER),
+    (dict(a_dtype=L.DT_F32, c_dtype=L.DT_F32), L.ERR_DTYPE),
+    (dict(c_dtype=L.DT_F16), L.ERR_DTYPE),
+    (dict(n_out=2, idx=P, idx_dtype=L.DT_BF16, ow=P, ow_dtype=L.DT_F16), L.ERR_DTYPE),
+    (dict(a=P + 8), L.ERR_ALIGNMENT),           # TMA needs a 16-byte aligned base
+    (dict(a_rs=132), L.ERR_ALIGNMENT),          # ... and a 16-byte row pitch
+    (dict(a_rs=64), L.ERR_ALIGNMENT),           # row pitch below K
+    (dict(packed=P + 4), L.ERR_ALIGNMENT),
+    (dict(w_rs=72), L.ERR_ALIGNMENT),
+    (dict(c_rs=100), L.ERR_STRIDE),
+    (dict(layout=3), L.ERR_UNSUPPORTED),
+])
+def test_gemm_rejects_bad_arguments_on_host(kw, code):
+    assert _gemm(**kw) == code
+
+
+def test_gemm_workspace_size_and_check():
+    lib = L.lib()
+    # 2 weight tiles, long K: split-K, needs counters + fp32 partials
+    need = lib.spectra_w4a16_gemm_workspace_bytes(16, 256, 16384, 0)
+    assert need >= 2 * 16 * 256 * 4
+    # enough tiles to fill the GPU: no split, no workspace
+    assert lib.spectra_w4a16_gemm_workspace_bytes(256, 65536, 4096, 0) == 0
+    assert lib.spectra_w4a16_gemm_workspace_bytes(0, 256, 128, 0) == 0
+    assert _gemm(N=256, c_rs=256, K=16384, a_rs=16384, w_rs=8192, s_rs=512, z_rs=512) == L.ERR_WORKSPACE
+    assert _gemm(N=256, c_rs=256, K=16384, a_rs=16384, w_rs=8192, s_rs=512, z_rs=512,
+                 ws=P, ws_bytes=need - 1) == L.ERR_WORKSPACE
+
+
 def test_status_strings_cover_all_codes():
     lib = L.lib()
     for code in range(0, 9):
@@ -113,3 +157,5 @@ def test_python_api_has_no_cpu_fallback():
         SK.fused_w4a16_gemv_hdsq(x, p, s, z, marlin_layout=True)
     with pytest.raises(RuntimeError, match="CUDA"):
         SK.dequantize(p, s, z)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        SK.batched_w4a16_gemm(x.repeat(4, 1), p, s, z, marlin_layout=True)
