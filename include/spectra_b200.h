@@ -145,6 +145,44 @@ SPECTRA_API int spectra_w4a16_gemm(
 /* Workspace bytes spectra_w4a16_gemm needs for this problem (0: none). */
 SPECTRA_API size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out);
 
+/*
+ * Allocation-free variant of spectra_w4a16_gemm.  It has no counterpart in the
+ * reference (spectra/kernels.py allocates its output and scratch through
+ * torch).  It is for callers that cannot allocate device memory or hand the
+ * GEMM a workspace: a host whose own arena already owns the device memory
+ * (a cudaMalloc there fails or synchronises the whole device in the middle
+ * of a forward pass), or a plugin interface that passes only the operands,
+ * like the reference's batched_w4a16_gemm signature (no workspace argument).
+ *
+ * Same arguments and results as spectra_w4a16_gemm, without the workspace:
+ * split-K scratch lives in one file-scope device array of
+ * SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES per device, and the call makes no
+ * cudaMalloc/cudaFree or other allocating call.
+ *   - Limit: a problem whose spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out)
+ *     exceeds SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES is rejected with
+ *     SPECTRA_ERR_WORKSPACE before anything launches.
+ *   - Zero state: the scratch's counters must be zero when a call starts.  The
+ *     array is zero when the module loads and every call leaves its counters
+ *     zero again, so the caller never clears anything.
+ *   - Setup: the first call on each device looks the array's address up with
+ *     cudaGetSymbolAddress (with that device current), which may load the
+ *     module; make that first call before any stream capture begins.
+ *   - Races: all calls on one device (all streams and host threads of the
+ *     process) share the one array, so calls that overlap in time race and
+ *     give wrong results.  Issue them one after another, e.g. on one stream.
+ */
+#define SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES 8388608  /* 8 MiB */
+
+SPECTRA_API int spectra_w4a16_gemm_noalloc(
+    const void* a, int a_dtype, int64_t a_row_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* c, int c_dtype, int64_t c_row_stride,
+    int64_t M, int64_t N, int64_t K, int layout, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -44,6 +44,16 @@ PROTOTYPES = {
         c_int64, c_int64, c_int64, c_int,              # M, N, K, layout
         c_void_p, c_size_t, c_void_p]),                # workspace, workspace_bytes, stream
     "spectra_w4a16_gemm_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "spectra_w4a16_gemm_noalloc": (c_int, [
+        c_void_p, c_int, c_int64,                      # a, a_dtype, a_row_stride
+        c_void_p, c_int64,                             # packed, w_row_stride
+        c_void_p, c_int64, c_int64,                    # scales
+        c_void_p, c_int64, c_int64,                    # zeros
+        c_void_p, c_int, c_int64,                      # outlier_idx, idx_dtype, n_out
+        c_void_p, c_int, c_int64, c_int64,             # outlier_w
+        c_void_p, c_int, c_int64,                      # c, c_dtype, c_row_stride
+        c_int64, c_int64, c_int64, c_int,              # M, N, K, layout
+        c_void_p]),                                    # stream
     "spectra_w4a16_dequant": (c_int, [
         c_void_p, c_int64,
         c_void_p, c_int64, c_int64,

@@ -171,6 +171,28 @@ int spectra_w4a16_gemm(
   return launch_gemm(g, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+int spectra_w4a16_gemm_noalloc(
+    const void* a, int a_dtype, int64_t a_row_stride,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride, int64_t s_col_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int64_t z_col_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
+    void* c, int c_dtype, int64_t c_row_stride,
+    int64_t M, int64_t N, int64_t K, int layout, void* stream) {
+  // the size limit is checked on the host before any CUDA call
+  if (spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out) > size_t(SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES))
+    return SPECTRA_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  const int st = gemm_noalloc_scratch(&scratch, &scratch_bytes);
+  if (st != SPECTRA_OK) return st;
+  return spectra_w4a16_gemm(a, a_dtype, a_row_stride, packed, w_row_stride, scales, s_row_stride, s_col_stride,
+                            zeros, z_row_stride, z_col_stride, outlier_idx, idx_dtype, n_out, outlier_w, ow_dtype,
+                            ow_row_stride, ow_col_stride, c, c_dtype, c_row_stride, M, N, K, layout, scratch,
+                            scratch_bytes, stream);
+}
+
 size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   return plan_gemm(M, N, K, n_out).workspace;

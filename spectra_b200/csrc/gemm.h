@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 namespace spectra {
 
@@ -29,5 +30,9 @@ struct GemmPlan {
 
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out);
 int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// Address and size of the static split-K scratch of the current device
+// (looked up once per device with cudaGetSymbolAddress).
+int gemm_noalloc_scratch(void** ptr, size_t* bytes);
 
 }  // namespace spectra

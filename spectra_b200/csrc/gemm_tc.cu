@@ -32,6 +32,11 @@
 #include "gemm.h"
 #include "sm100_ptx.cuh"
 
+// Split-K scratch of spectra_w4a16_gemm_noalloc, laid out like a caller
+// workspace (tile counters, then fp32 partials).  Zero when the module loads;
+// every GEMM leaves its counters zero again.
+static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES];
+
 namespace spectra {
 
 namespace {
@@ -470,6 +475,23 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   }
   kern<<<dim3(unsigned(pl.tiles_n * pl.S), unsigned(pl.m_chunks)), kThreads, pl.smem, st>>>(mw, ma, kp);
   return cuda_status(cudaGetLastError());
+}
+
+int gemm_noalloc_scratch(void** ptr, size_t* bytes) {
+  static std::atomic<void*> addr[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    e = cudaGetSymbolAddress((void**)&p, g_gemm_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    addr[dev].store(p, std::memory_order_release);
+  }
+  *ptr = p;
+  *bytes = sizeof(g_gemm_noalloc_scratch);
+  return SPECTRA_OK;
 }
 
 }  // namespace spectra
