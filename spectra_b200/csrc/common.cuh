@@ -28,6 +28,10 @@ bool pdl_enabled();
 // SPECTRA_B200_GEMV_MMA=0, which selects the exact CUDA-core kernel).
 bool mma_path_enabled();
 
+// GEMM scales / zero points fetched by tensor map when their layout allows
+// (on unless SPECTRA_B200_GEMM_SZ_TMA=0, which forces the plain-load path).
+bool sz_tma_enabled();
+
 inline int cuda_status(cudaError_t e) {
   if (e != cudaSuccess) {
     set_last_cuda_error(e);

@@ -23,7 +23,11 @@ struct GemmArgs {
 };
 
 struct GemmPlan {
-  int MT, m_chunks, tiles_n, nk, n_os, S, stages, act_stage_bytes;
+  int MT, m_chunks, tiles_n;
+  int nk, ncs, n_os;          // 64-k MMA steps, 256-k code stages, 64-column outlier steps
+  int S;                      // K splits per tile
+  int act_stages, code_stages, act_stage_bytes;
+  int issuers;                // warps issuing MMAs (each with its own accumulator)
   uint32_t tmem_cols;
   size_t smem, workspace;
 };

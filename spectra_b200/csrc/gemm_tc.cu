@@ -9,24 +9,36 @@
 // Swap-AB: the MMA's M dimension is 128 weight rows, its N dimension the
 // tokens (a multiple of 16, <= 256), so M = 16 wastes nothing.
 //
-// CTA = 10 warps: warp 0 issues TMA loads (packed codes, activations), warp 1
-// owns TMEM and issues the MMAs, warps 2..9 dequantise and run the epilogue.
-// Per 64-k stage:
-//   producer : packed codes [128 rows x 32 B] and activations [MT x 128 B,
-//              128B-swizzled, K-major] land in shared memory (mbarrier tx).
-//   dequant  : thread (row r = its TMEM lane, half h) turns one 32-code group
-//              into 16 bf16x2 words of exact (q - z) * s rounded to nearest
-//              even, tcgen05.st into the stage's A columns of TMEM.
-//   MMA      : tcgen05.mma kind::f16, A from TMEM, B from shared memory,
-//              D (fp32, 128 lanes x MT columns) in TMEM; tcgen05.commit frees
-//              the stage.
-// Outlier columns become extra stages: the dequant warps gather a[:, idx]
-// into the B stage (same swizzled layout) and convert ow rows into the A
-// stage.  K is split across CTAs when there are too few weight tiles to fill
-// the GPU; the last CTA of a tile sums the fp32 partials in split order
-// (deterministic) and resets the tile's counter for the next call.
+// CTA = 14 warps: warp 0 streams weights, warp 10 streams activations, warp 1
+// owns TMEM, warps 1 and 11..13 issue the MMAs (as many as the token tile
+// needs), warps 2..9 dequantise and run the epilogue.
+// Every copy engine here is limited by requests (row segments), not bytes, so
+// each stream is fetched in the widest rows it has:
+//   code ring  : packed codes [128 rows x 128 B = 256 k] per stage, one TMA
+//                box, 128B-swizzled.
+//   sz ring    : scales [128 rows x 64 groups = 128 B] and zero points
+//                [128 rows x 64 B] per 2048 k, TMA boxes swizzled 128B / 64B
+//                (when their strides allow a tensor map; else the dequant
+//                warps read them from global memory one code stage ahead).
+//   act ring   : activations [MT x 64 k, 128B-swizzled, K-major] per MMA step
+//                by TMA.
+//   dequant    : thread (row r = its TMEM lane, half h) turns one 32-code
+//                group per 64-k step into 16 bf16x2 words of exact
+//                (q - z) * s rounded to nearest even, tcgen05.st into one of
+//                four A slots of TMEM.
+//   MMA        : tcgen05.mma kind::f16, A from TMEM, B from shared memory,
+//                D (fp32, 128 lanes x MT columns) in TMEM; tcgen05.commit
+//                frees the act slot and the A slot.
+// Outlier columns become extra 64-column steps: the dequant warps gather
+// a[:, idx] into the act slot (same swizzled layout) and convert ow rows into
+// the A slot.  K is split across CTAs (in 256-k code stages) when there are too
+// few weight tiles to fill the GPU; the last CTA of a tile sums the fp32
+// partials in split order (deterministic) and resets the tile's counter for
+// the next call.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "gemm.h"
@@ -43,12 +55,25 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kRows = 128;     // weight rows per tile (MMA M)
-constexpr int kBK = 64;        // k per stage (4 MMAs of K=16)
-constexpr int kWarps = 10;
+constexpr int kRows = 128;                           // weight rows per tile (MMA M)
+constexpr int kStep = 64;                            // k per MMA step (4 MMAs of K=16)
+constexpr int kCodeK = 256;                          // k per code stage
+constexpr int kStepsPerCode = kCodeK / kStep;        // 4
+constexpr int kCodeBytes = kRows * kCodeK / 2;       // 16 KB of packed codes
+constexpr int kSzGroups = 64;                        // groups per sz chunk (2048 k)
+constexpr int kCodesPerSz = kSzGroups * kGroup / kCodeK;  // 8 code stages
+constexpr int kSzScaleBytes = kRows * kSzGroups * 2; // 16 KB
+constexpr int kSzZeroBytes = kRows * kSzGroups;      // 8 KB
+constexpr int kSzSlot = kSzScaleBytes + kSzZeroBytes;
+constexpr int kSzSlots = 2;
+constexpr int kWarps = 14;       // 0 weights, 1 + 11..13 MMA issuers, 2..9 dequant, 10 activations
 constexpr int kDeqWarps = 8;
+constexpr int kActWarp = 10;
+constexpr int kMaxIssuers = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxMT = 256;
+constexpr int kDone = 8;                             // units tracked by the MMA-done barrier ring
+constexpr int kMaxActStages = 16;
 constexpr size_t kMaxDynSmem = 200 * 1024;
 
 __device__ int g_gemm_timeouts;  // stuck pipeline waits since load (diagnostic)
@@ -56,17 +81,17 @@ __device__ int g_gemm_timeouts;  // stuck pipeline waits since load (diagnostic)
 struct GemmKParams {
   const __half* scales; int64_t s_rs, s_cs;
   const uint8_t* zeros; int64_t z_rs, z_cs;
-  const void* a; int64_t a_rs;  // activations (outlier gather)
+  const void* a; int64_t a_rs;
   const void* idx; int idx_dtype; int n_out;
   const void* ow; int ow_dtype; int64_t ow_rs, ow_cs;
   void* c; int c_dtype; int64_t c_rs;
   float* partials;  // [S][M][N] when S > 1
   int* counters;    // [tiles_n * m_chunks]
   int M, N, K, layout;
-  int MT, stages, S, nk, n_os, tiles_n;
-  uint32_t idesc;
-  uint32_t tmem_cols;
-  int off_act, act_stage_bytes, off_w, off_bar;
+  int MT, S, nk, ncs, n_os, tiles_n;
+  int act_stages, code_stages, issuers;
+  uint32_t idesc, tmem_cols;
+  int off_act, act_stage_bytes, off_code, off_sz, off_bar;
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
@@ -119,6 +144,63 @@ __device__ __forceinline__ void dequant_group(const uint4 w, float s, float z, i
   }
 }
 
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t m, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(c));  // (a & m) | c
+  return r;
+}
+
+// Marlin group (byte j: k = j low nibble, k = j + 16 high nibble) -> 16 words
+// of two 16-bit floats, done in packed 16-bit arithmetic.  Bytes j, j+1 are
+// spread to the two halves of a word (PRMT); a low nibble then becomes the
+// 16-bit float 128 + q (bf16) / 1024 + q (fp16) by one AND-OR, a high nibble
+// (shifted) 16 + q / 1024 + q.  Subtracting the same offset plus z is exact.
+//   fp16: (q - z) * s is one multiply, rounded once.
+//   bf16: s (fp16, 11 significant bits) = s_hi + s_lo with s_hi = bf16(s) and
+//         s_lo exact in bf16 (at most 3 significant bits); (q - z) * s_lo is
+//         exact (at most 7 bits) and fma(q - z, s_hi, (q - z) * s_lo) rounds
+//         the exact (q - z) * s once.
+// Both give the same bits as rounding the exact fp32 (q - z) * s.
+template <bool BF16>
+__device__ __forceinline__ void dequant_marlin(const uint4 w, float s, float z, uint32_t (&out)[16]) {
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  if constexpr (BF16) {
+    const __nv_bfloat16 shi = __float2bfloat16_rn(s);
+    const __nv_bfloat16 slo = __float2bfloat16_rn(s - __bfloat162float(shi));
+    const __nv_bfloat162 S_hi = __bfloat162bfloat162(shi), S_lo = __bfloat162bfloat162(slo);
+    const __nv_bfloat162 Z_lo = __bfloat162bfloat162(__float2bfloat16_rn(128.f + z));
+    const __nv_bfloat162 Z_hi = __bfloat162bfloat162(__float2bfloat16_rn(16.f + z));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t A = __byte_perm(words[j], 0, 0x4140), B = __byte_perm(words[j], 0, 0x4342);
+      const uint32_t p[4] = {and_or(A, 0x000F000Fu, 0x43004300u), and_or(B, 0x000F000Fu, 0x43004300u),
+                             and_or(A >> 1, 0x00780078u, 0x41804180u), and_or(B >> 1, 0x00780078u, 0x41804180u)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 P = *reinterpret_cast<const __nv_bfloat162*>(&p[i]);
+        const __nv_bfloat162 qz = __hsub2(P, i < 2 ? Z_lo : Z_hi);
+        const __nv_bfloat162 r = __hfma2(qz, S_hi, __hmul2(qz, S_lo));
+        out[(i < 2 ? 0 : 8) + 2 * j + (i & 1)] = *reinterpret_cast<const uint32_t*>(&r);
+      }
+    }
+  } else {
+    const __half2 S = __half2half2(__float2half_rn(s));
+    const __half2 Z = __half2half2(__float2half_rn(1024.f + z));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t A = __byte_perm(words[j], 0, 0x4140), B = __byte_perm(words[j], 0, 0x4342);
+      const uint32_t p[4] = {and_or(A, 0x000F000Fu, 0x64006400u), and_or(B, 0x000F000Fu, 0x64006400u),
+                             and_or(A >> 4, 0x000F000Fu, 0x64006400u), and_or(B >> 4, 0x000F000Fu, 0x64006400u)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 P = *reinterpret_cast<const __half2*>(&p[i]);
+        const __half2 r = __hmul2(__hsub2(P, Z), S);
+        out[(i < 2 ? 0 : 8) + 2 * j + (i & 1)] = *reinterpret_cast<const uint32_t*>(&r);
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ uint16_t to16(float v, bool bf16) {
   if (bf16) {
     const __nv_bfloat16 b = __float2bfloat16_rn(v);
@@ -132,18 +214,26 @@ __device__ __forceinline__ uint16_t load_act16(const void* a, int64_t i) {
   return __ldg(reinterpret_cast<const unsigned short*>(a) + i);
 }
 
-template <bool BF16>
+template <bool BF16, bool SZ_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_w4a16_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+    gemm_w4a16_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
+                         const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_a,
                          const __grid_constant__ GemmKParams kp) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* act_st = smem + kp.off_act;   // [stages][MT x 128 B], 1024-aligned
-  uint8_t* w_st = smem + kp.off_w;       // [stages][128 x 32 B]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kp.off_bar);
-  uint64_t* aready = full + kp.stages;
-  uint64_t* mdone = aready + kp.stages;
-  uint64_t* accf = mdone + kp.stages;
+  const int AS = kp.act_stages, CS = kp.code_stages, NI = kp.issuers;
+  uint8_t* act_st = smem + kp.off_act;     // [AS][MT x 128 B]
+  uint8_t* code_st = smem + kp.off_code;   // [CS][128 x 128 B]
+  uint8_t* sz_st = smem + kp.off_sz;       // [2][scales 128 x 128 B | zeros 128 x 64 B]
+  uint64_t* cfull = reinterpret_cast<uint64_t*>(smem + kp.off_bar);  // [CS] code stage landed
+  uint64_t* cfree = cfull + CS;                                       // [CS] code stage read (8 warps)
+  uint64_t* szfull = cfree + CS;                                      // [2] sz chunk landed
+  uint64_t* szfree = szfull + kSzSlots;                               // [2] sz chunk read (8 warps)
+  uint64_t* afull = szfree + kSzSlots;                                // [AS] act slot landed / filled
+  uint64_t* afree = afull + AS;                                       // [AS] act slot consumed by MMAs
+  uint64_t* aready = afree + AS;                                      // [2] A slot written (8 warps)
+  uint64_t* mdone = aready + 2;                                       // [kDone] unit's MMAs complete (NI)
+  uint64_t* accf = mdone + kDone;                                     // accumulators final (NI)
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_last;
@@ -155,193 +245,401 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int mchunk = blockIdx.y;
   const int n0 = tile * kRows;
   const int m0 = mchunk * kp.MT;
-  // main k-stages of this split (balanced, never empty since S <= nk), then
-  // (last split only) the outlier stages
-  const int it0 = int(int64_t(split) * kp.nk / kp.S);
-  const int it1 = int(int64_t(split + 1) * kp.nk / kp.S);
-  const int n_main = it1 - it0;
+  // This split's code stages [cs0, cs1) (balanced, never empty since S <= ncs)
+  // and its main 64-k steps, then (last split only) the outlier steps.  The
+  // unit of work between the dequant warps and the MMA issuers is one code
+  // stage (up to 4 steps; fewer at the K tail), then units of up to 4 outlier
+  // steps.
+  const int cs0 = int(int64_t(split) * kp.ncs / kp.S);
+  const int cs1 = int(int64_t(split + 1) * kp.ncs / kp.S);
+  const int n_code = cs1 - cs0;
+  const int st0 = cs0 * kStepsPerCode;
+  const int n_main = min(kp.nk, cs1 * kStepsPerCode) - st0;
   const int n_out_st = (split == kp.S - 1) ? kp.n_os : 0;
   const int n_it = n_main + n_out_st;
+  const int n_units = n_code + (n_out_st + kStepsPerCode - 1) / kStepsPerCode;
+  auto steps_of = [&](int u) {
+    return u < n_code ? min(kStepsPerCode, n_main - u * kStepsPerCode)
+                      : min(kStepsPerCode, n_out_st - (u - n_code) * kStepsPerCode);
+  };
+  auto step_of = [&](int u, int j) {
+    return u < n_code ? u * kStepsPerCode + j : n_main + (u - n_code) * kStepsPerCode + j;
+  };
+  auto unit_of = [&](int st) { return st < n_main ? st / kStepsPerCode : n_code + (st - n_main) / kStepsPerCode; };
+  const uint32_t act_bytes = uint32_t(kp.act_stage_bytes);
+  auto act_slot = [&](int u, int j) -> uint8_t* { return act_st + (step_of(u, j) % AS) * act_bytes; };
+  // sz chunk (local index) of local code stage lc
+  const int sz0 = cs0 / kCodesPerSz;
+  auto sz_of = [&](int lc) { return (cs0 + lc) / kCodesPerSz - sz0; };
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int i = 0; i < kp.stages; ++i) {
-      mbar_init(full + i, 1);
-      mbar_init(aready + i, kDeqWarps);
-      mbar_init(mdone + i, 1);
+    for (int i = 0; i < CS; ++i) {
+      mbar_init(cfull + i, 1);
+      mbar_init(cfree + i, kDeqWarps);
     }
-    mbar_init(accf, 1);
+    for (int i = 0; i < kSzSlots; ++i) {
+      mbar_init(szfull + i, 1);
+      mbar_init(szfree + i, kDeqWarps);
+    }
+    for (int i = 0; i < AS; ++i) {
+      mbar_init(afull + i, 1);
+      mbar_init(afree + i, NI);  // one commit per MMA issuer
+    }
+    for (int i = 0; i < 2; ++i) mbar_init(aready + i, kDeqWarps);
+    for (int i = 0; i < kDone; ++i) mbar_init(mdone + i, NI);  // one commit per MMA issuer
+    mbar_init(accf, NI);
     fence_mbar_init();
   }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_w);
+    if constexpr (SZ_TMA) {
+      prefetch_tensormap(&map_s);
+      prefetch_tensormap(&map_z);
+    }
+    prefetch_tensormap(&map_a);
+  }
+  __syncthreads();
+
+  // weight producer (warp 0, lane 0): code stage lc -> slot lc % CS, preceded by
+  // its sz chunk when lc starts one.  Returns false if a wait gave up.
+  auto issue_weights = [&](int lc, bool may_wait) -> bool {
+    if constexpr (SZ_TMA) {
+      const int ch = sz_of(lc);
+      if (lc == 0 || ch != sz_of(lc - 1)) {
+        if (ch >= kSzSlots && !(may_wait && mbar_wait(szfree + ch % kSzSlots, uint32_t((ch / kSzSlots - 1) & 1), &s_abort)))
+          return false;
+        uint8_t* slot = sz_st + (ch % kSzSlots) * kSzSlot;
+        uint64_t* bar = szfull + ch % kSzSlots;
+        mbar_arrive_expect_tx(bar, uint32_t(kSzSlot));
+        tma_load_2d(slot, &map_s, (sz0 + ch) * kSzGroups, n0, bar);
+        tma_load_2d(slot + kSzScaleBytes, &map_z, (sz0 + ch) * kSzGroups, n0, bar);
+      }
+    }
+    if (lc >= CS && !(may_wait && mbar_wait(cfree + lc % CS, uint32_t((lc / CS - 1) & 1), &s_abort))) return false;
+    mbar_arrive_expect_tx(cfull + lc % CS, uint32_t(kCodeBytes));
+    tma_load_2d(code_st + (lc % CS) * kCodeBytes, &map_w, (cs0 + lc) * (kCodeK / 2), n0, cfull + lc % CS);
+    return true;
+  };
+  // The packed codes, scales and zero points are constant weights, never
+  // written by a kernel this one depends on: their first stages are requested
+  // before the dependency wait (the first CS code stages span at most two sz
+  // chunks, so nothing here waits).
+  const int pre = min(CS, n_code);
+  if (warp == 0 && lane == 0)
+    for (int lc = 0; lc < pre; ++lc) issue_weights(lc, false);
+  pdl_wait();
+  // TMEM is taken only after the wait, so a CTA waiting on the previous grid
+  // never holds tensor memory that grid's CTAs could need.
   if (warp == 1) {
     tmem_alloc(&s_tmem, kp.tmem_cols);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&map_w);
-    prefetch_tensormap(&map_a);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem = s_tmem;
-  const uint32_t a_col0 = uint32_t(kp.MT);  // A stages follow the accumulator's MT columns
-  const uint32_t act_bytes = uint32_t(kp.act_stage_bytes);
+  // TMEM columns: one fp32 accumulator [128 x MT] per MMA issuer, then two A
+  // slots of 128 columns (one unit = 4 steps x 32 columns each)
+  const uint32_t a_col0 = uint32_t(NI * kp.MT);
   const bool bf16 = BF16;
+  const int zero_flag = 0;
+  auto done_parity = [](int u) { return uint32_t((u / kDone) & 1); };
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- weight producer
     if (lane == 0) {
-      int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it % kp.stages;
-        const int r = it / kp.stages;
-        if (r > 0 && !mbar_wait(mdone + s, uint32_t((r - 1) & 1), &s_abort)) { s_abort = 1; atomicAdd(&g_gemm_timeouts, 1); break; }
-        issued = it + 1;
-        if (it < n_main) {
-          const int kk = (it0 + it) * kBK;
-          mbar_arrive_expect_tx(full + s, 4096u + act_bytes);
-          tma_load_2d(w_st + s * 4096, &map_w, kk / 2, n0, full + s);
-          tma_load_2d(act_st + s * act_bytes, &map_a, kk, m0, full + s);
-        } else {
-          mbar_arrive(full + s);  // outlier stage: the dequant warps fill B themselves
-        }
-      }
-      // Before the CTA may exit, every TMA copy it issued must have landed: wait
-      // (bounded, ignoring the abort flag) for the last use of each stage.
-      // On the normal path these phases completed long ago.
-      const int zero = 0;
-      for (int it = max(0, issued - kp.stages); it < issued; ++it)
-        mbar_wait(full + it % kp.stages, uint32_t((it / kp.stages) & 1), &zero);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issue
-    if (lane == 0) {
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it % kp.stages;
-        const uint32_t par = uint32_t((it / kp.stages) & 1);
-        if (!mbar_wait(aready + s, par, &s_abort) || !mbar_wait(full + s, par, &s_abort)) {
+      int issued = pre;
+      for (int lc = pre; lc < n_code; ++lc) {
+        if (!issue_weights(lc, true)) {
           s_abort = 1;
           atomicAdd(&g_gemm_timeouts, 1);
           break;
         }
-        tc_fence_after();
-        const uint32_t b_base = smem_u32(act_st + s * act_bytes);
-#pragma unroll
-        for (int k16 = 0; k16 < kBK / 16; ++k16) {
-          const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
-          mma_ts(tmem, tmem + a_col0 + uint32_t(s * 32 + k16 * 8), bdesc, kp.idesc, (it > 0 || k16 > 0) ? 1u : 0u);
+        issued = lc + 1;
+      }
+      // every TMA copy issued must land before the CTA may exit (bounded wait,
+      // ignoring the abort flag); on the normal path these completed long ago
+      for (int lc = max(0, issued - CS); lc < issued; ++lc)
+        mbar_wait(cfull + lc % CS, uint32_t((lc / CS) & 1), &zero_flag);
+      if constexpr (SZ_TMA) {
+        if (issued > 0) {
+          const int last = sz_of(issued - 1);
+          for (int ch = max(0, last - kSzSlots + 1); ch <= last; ++ch)
+            mbar_wait(szfull + ch % kSzSlots, uint32_t((ch / kSzSlots) & 1), &zero_flag);
         }
-        mma_commit(mdone + s);
+      }
+    }
+  } else if (warp == kActWarp) {
+    // ---------------------------------------------------------------- activation producer
+    // activations [MT x 64 k] per step by TMA; slots recycle per step (a unit
+    // may have more steps than there are slots)
+    if (lane == 0) {
+      int issued = 0;
+      for (int st = 0; st < n_it; ++st) {
+        const int sa = st % AS;
+        if (st >= AS && !mbar_wait(afree + sa, uint32_t((st / AS - 1) & 1), &s_abort)) {
+          s_abort = 1;
+          atomicAdd(&g_gemm_timeouts, 1);
+          break;
+        }
+        if (st < n_main) {
+          mbar_arrive_expect_tx(afull + sa, act_bytes);
+          tma_load_2d(act_st + sa * act_bytes, &map_a, (st0 + st) * kStep, m0, afull + sa);
+        } else {
+          mbar_arrive(afull + sa);  // outlier step: the dequant warps fill the slot
+        }
+        issued = st + 1;
+      }
+      for (int st = max(0, issued - AS); st < issued; ++st)
+        mbar_wait(afull + st % AS, uint32_t((st / AS) & 1), &zero_flag);
+    }
+  } else if (warp == 1 || warp > kActWarp) {
+    // ---------------------------------------------------------------- MMA issue
+    // One elected thread can start a tcgen05.mma only every ~50 cycles and
+    // each commit / wait costs tens of cycles more, so the MMAs of a whole
+    // unit (16) are issued between one wait and one commit, and for small MT
+    // they are spread over several warps, each accumulating its own K-slice
+    // (k16 = issuer, issuer + NI, ...) into its own accumulator.
+    const int issuer = warp == 1 ? 0 : warp - kActWarp;
+    if (issuer < NI && lane == 0) {
+      const uint32_t d_tmem = tmem + uint32_t(issuer * kp.MT);
+      bool live = true;
+      for (int u = 0; u < n_units && live; ++u) {
+        const int ns = steps_of(u);
+        if (!mbar_wait(aready + (u & 1), uint32_t((u >> 1) & 1), &s_abort)) {
+          s_abort = 1;
+          atomicAdd(&g_gemm_timeouts, 1);
+          live = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_unit = tmem + a_col0 + uint32_t((u & 1) * 128);
+        for (int j = 0; j < ns && live; ++j) {
+          const int st = step_of(u, j);
+          if (!mbar_wait(afull + st % AS, uint32_t((st / AS) & 1), &s_abort)) {
+            s_abort = 1;
+            atomicAdd(&g_gemm_timeouts, 1);
+            live = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(act_slot(u, j));
+          for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
+            const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
+            mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
+                   (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+          }
+          mma_commit(afree + st % AS);
+        }
+        if (!live) break;
+        mma_commit(mdone + u % kDone);
       }
       mma_commit(accf);
     }
   } else {
     // ---------------------------------------------------------------- dequant + epilogue
     const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int h = (warp - 2) >> 2;     // which half of the 64-k stage (one group)
+    const int h = (warp - 2) >> 2;     // which group of each 64-k step
     const int row = q * 32 + lane;     // weight row within the tile
     const int64_t n = int64_t(n0) + row;
     const bool nv = n < kp.N;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     const int G = kp.K / kGroup;
-    // scale / zero of the next main stage, loaded one stage ahead
-    auto sz = [&](int it, float& sv, float& zv) {
-      const int g = (it0 + it) * 2 + h;
-      if (nv && it < n_main && g < G) {
-        sv = __half2float(__ldg(kp.scales + n * kp.s_rs + int64_t(g) * kp.s_cs));
-        zv = float(__ldg(kp.zeros + n * kp.z_rs + int64_t(g) * kp.z_cs));
-      } else {
-        sv = 0.f;
-        zv = 0.f;
+
+    // the warp leaves the pipeline (warp-uniformly) when a wait gave up; only
+    // lane 0 polls, the vote hands the result (and the ordering) to the warp
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const bool ok = __all_sync(0xffffffffu, lane == 0 ? mbar_wait(bar, parity, &s_abort) : true);
+      if (!ok && lane == 0) {
+        s_abort = 1;
+        atomicAdd(&g_gemm_timeouts, 1);
+      }
+      return ok;
+    };
+    // this unit's A slot written: hand it to the MMA issuers
+    auto publish = [&](int u) {
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(aready + (u & 1));
+    };
+
+    // scale / zero point of this row for the four groups 2j+h of code stage lc
+    // (global-memory path, used when they cannot be fetched by tensor map)
+    auto load_sz = [&](int lc, float (&sv)[4], float (&zv)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int g = (cs0 + lc) * 8 + 2 * j + h;
+        if (nv && lc < n_code && g < G) {
+          sv[j] = __half2float(__ldg(kp.scales + n * kp.s_rs + int64_t(g) * kp.s_cs));
+          zv[j] = float(__ldg(kp.zeros + n * kp.z_rs + int64_t(g) * kp.z_cs));
+        } else {
+          sv[j] = 0.f;
+          zv[j] = 0.f;
+        }
       }
     };
-    float s_next, z_next;
-    sz(0, s_next, z_next);
-    for (int it = 0; it < n_it; ++it) {
-      const int s = it % kp.stages;
-      const int r = it / kp.stages;
-      float sv = s_next, zv = z_next;
-      sz(it + 1, s_next, z_next);
-      // the wait result is made warp-uniform: tcgen05.st below is .aligned
-      bool got = mbar_wait(full + s, uint32_t(r & 1), &s_abort);
-      if (got && r > 0) got = mbar_wait(mdone + s, uint32_t((r - 1) & 1), &s_abort);
-      if (!__all_sync(0xffffffffu, got)) {
-        if (lane == 0) { s_abort = 1; atomicAdd(&g_gemm_timeouts, 1); }
-        break;
-      }
-      tc_fence_after();
-      uint32_t vals[16];
-      if (it < n_main) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(w_st + s * 4096 + row * 32 + h * 16);
-        dequant_group<BF16>(wv, sv, zv, kp.layout, vals);
-      } else {
-        // outlier stage o: columns j0 .. j0+63 of ow / of a[:, idx]
-        const int j0 = (it - n_main) * kBK;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float lo = 0.f, hi = 0.f;
-          const int j = j0 + h * 32 + 2 * c;
-          if (nv && j < kp.n_out) lo = load_as_float(kp.ow, n * kp.ow_rs + int64_t(j) * kp.ow_cs, kp.ow_dtype);
-          if (nv && j + 1 < kp.n_out) hi = load_as_float(kp.ow, n * kp.ow_rs + int64_t(j + 1) * kp.ow_cs, kp.ow_dtype);
-          vals[c] = pack2<BF16>(lo, hi);
+    float s_next[4], z_next[4];
+    if constexpr (!SZ_TMA) load_sz(0, s_next, z_next);
+
+    bool alive = true;
+    auto main_units = [&](auto marlin_tag) {
+      constexpr bool kMarlin = decltype(marlin_tag)::value;
+      for (int lc = 0; lc < n_code && alive; ++lc) {
+        const int c = lc % CS;
+        const uint8_t* slot = code_st + c * kCodeBytes;
+        const int ch = sz_of(lc);
+        const bool first_of_sz = (lc == 0 || ch != sz_of(lc - 1));
+        const bool last_of_sz = (lc == n_code - 1 || ch != sz_of(lc + 1));
+        // A slot free (MMAs of unit lc - 2 done), codes and sz landed
+        if ((lc >= 2 && !wait_all(mdone + (lc - 2) % kDone, done_parity(lc - 2))) ||
+            !wait_all(cfull + c, uint32_t((lc / CS) & 1)) ||
+            (SZ_TMA && first_of_sz && !wait_all(szfull + ch % kSzSlots, uint32_t((ch / kSzSlots) & 1)))) {
+          alive = false;
+          break;
         }
-        // gather a[m0+m, idx[j0+jj]] into the B stage, 128B-swizzled K-major
-        uint8_t* bst = act_st + s * act_bytes;
+        tc_fence_after();
+        float sv[4], zv[4];
+        if constexpr (SZ_TMA) {
+          // this code stage's 8 groups: one 16-byte chunk of the row's 128-byte
+          // scale line (128B swizzle) and 8 bytes of its 64-byte zero line (64B
+          // swizzle: 16-byte chunk c of row r at c ^ ((r >> 1) & 3))
+          const uint8_t* sslot = sz_st + (ch % kSzSlots) * kSzSlot;
+          const int gi = (cs0 + lc) % kCodesPerSz;  // 8-group block within the chunk
+          const uint4 s8 = *reinterpret_cast<const uint4*>(sslot + row * 128 + ((gi ^ (row & 7)) << 4));
+          const uint2 z8 = *reinterpret_cast<const uint2*>(sslot + kSzScaleBytes + row * 64 +
+                                                           (((gi >> 1) ^ ((row >> 1) & 3)) << 4) + (gi & 1) * 8);
+          const uint32_t sw[4] = {s8.x, s8.y, s8.z, s8.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t hw = h ? (sw[j] >> 16) : (sw[j] & 0xFFFFu);
+            sv[j] = __half2float(__ushort_as_half(static_cast<unsigned short>(hw)));
+            const int b = 2 * j + h;
+            zv[j] = float(((b < 4 ? z8.x : z8.y) >> ((b & 3) * 8)) & 0xFFu);
+          }
+          if (last_of_sz) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(szfree + ch % kSzSlots);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sv[j] = s_next[j];
+            zv[j] = z_next[j];
+          }
+          load_sz(lc + 1, s_next, z_next);
+        }
+        const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t((lc & 1) * 128);
+        const int ns = steps_of(lc);
+#pragma unroll
+        for (int j = 0; j < kStepsPerCode; ++j) {
+          if (j < ns) {  // K tail (warp-uniform)
+            const int chunk = (2 * j + h) ^ (row & 7);  // 128B swizzle of the code tile
+            const uint4 wv = *reinterpret_cast<const uint4*>(slot + row * 128 + chunk * 16);
+            uint32_t vals[16];
+            if constexpr (kMarlin)
+              dequant_marlin<BF16>(wv, sv[j], zv[j], vals);
+            else
+              dequant_group<BF16>(wv, sv[j], zv[j], SPECTRA_LAYOUT_EVEN_ODD, vals);
+            tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
+          }
+        }
+        publish(lc);
+        // this code stage has been read: hand the slot back to the producer
+        if (lane == 0) mbar_arrive(cfree + c);
+      }
+    };
+    if (kp.layout == SPECTRA_LAYOUT_MARLIN)
+      main_units(std::true_type{});
+    else
+      main_units(std::false_type{});
+
+    // outlier units: columns j0 .. j0+63 of ow / of a[:, idx] per step
+    for (int u = n_code; u < n_units && alive; ++u) {
+      bool ok = u < 2 || wait_all(mdone + (u - 2) % kDone, done_parity(u - 2));
+      const int ns = steps_of(u);
+      for (int j = 0; j < ns && ok; ++j) {
+        const int st = step_of(u, j);
+        ok = wait_all(afull + st % AS, uint32_t((st / AS) & 1));
+      }
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t((u & 1) * 128);
+      for (int j = 0; j < ns; ++j) {
+        const int j0 = (step_of(u, j) - n_main) * kStep;
+        uint32_t vals[16];
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          float lo = 0.f, hi = 0.f;
+          const int jo = j0 + h * 32 + 2 * cc;
+          if (nv && jo < kp.n_out) lo = load_as_float(kp.ow, n * kp.ow_rs + int64_t(jo) * kp.ow_cs, kp.ow_dtype);
+          if (nv && jo + 1 < kp.n_out) hi = load_as_float(kp.ow, n * kp.ow_rs + int64_t(jo + 1) * kp.ow_cs, kp.ow_dtype);
+          vals[cc] = pack2<BF16>(lo, hi);
+        }
+        // gather a[m0+m, idx[j0+jj]] into the act slot, 128B-swizzled K-major
+        uint8_t* bst = act_slot(u, j);
         const int tid_d = (warp - 2) * 32 + lane;
-        for (int e = tid_d; e < kp.MT * kBK; e += kDeqWarps * 32) {
-          const int m = e / kBK, jj = e % kBK;
+        for (int e = tid_d; e < kp.MT * kStep; e += kDeqWarps * 32) {
+          const int m = e / kStep, jj = e % kStep;
           uint16_t v = 0;
-          const int j = j0 + jj;
-          if (m0 + m < kp.M && j < kp.n_out) {
-            const int64_t k = load_index(kp.idx, j, kp.idx_dtype);
+          const int jo = j0 + jj;
+          if (m0 + m < kp.M && jo < kp.n_out) {
+            const int64_t k = load_index(kp.idx, jo, kp.idx_dtype);
             if (k >= 0 && k < kp.K) v = load_act16(kp.a, int64_t(m0 + m) * kp.a_rs + k);
           }
           const int chunk = (jj >> 3) ^ (m & 7);
           *reinterpret_cast<uint16_t*>(bst + m * 128 + chunk * 16 + (jj & 7) * 2) = v;
         }
-        fence_proxy_async_smem();
+        tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
       }
-      tmem_st_x16(tmem + lane_base + a_col0 + uint32_t(s * 32 + h * 16), vals);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(aready + s);
+      fence_proxy_async_smem();
+      publish(u);
     }
 
     // ---------------------------------------------------------------- epilogue
-    // n_it == 0 cannot happen (S <= nk), but an empty split would leave the
-    // accumulator unwritten: treat it as zero.
+    // n_it == 0 cannot happen (S <= ncs), but an empty split would leave the
+    // accumulators unwritten: treat them as zero.
     const bool ok = mbar_wait(accf, 0u, &s_abort) && n_it > 0;
     tc_fence_after();
     const int half_cols = kp.MT / 2;
-    const int64_t nrow = int64_t(n0) + row;
+    // accumulator columns c0..c0+7, summed over the issuers in order
+    auto acc8 = [&](int c0, float (&v)[8]) {
+      tmem_ld_x8(tmem + lane_base + uint32_t(c0), v);
+      for (int i = 1; i < NI; ++i) {
+        float u8[8];
+        tmem_ld_x8(tmem + lane_base + uint32_t(i * kp.MT + c0), u8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] += u8[e];
+      }
+    };
     if (kp.S == 1) {
       for (int c0 = h * half_cols; c0 < (h + 1) * half_cols; c0 += 8) {
         float v[8];
-        tmem_ld_x8(tmem + lane_base + uint32_t(c0), v);
+        acc8(c0, v);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int m = m0 + c0 + i;
-          if (nv && m < kp.M)
-            reinterpret_cast<uint16_t*>(kp.c)[int64_t(m) * kp.c_rs + nrow] = to16(ok ? v[i] : 0.f, bf16);
+          if (nv && m < kp.M) reinterpret_cast<uint16_t*>(kp.c)[int64_t(m) * kp.c_rs + n] = to16(ok ? v[i] : 0.f, bf16);
         }
       }
     } else {
       float* part = kp.partials + int64_t(split) * kp.M * kp.N;
       for (int c0 = h * half_cols; c0 < (h + 1) * half_cols; c0 += 8) {
         float v[8];
-        tmem_ld_x8(tmem + lane_base + uint32_t(c0), v);
+        acc8(c0, v);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int m = m0 + c0 + i;
-          if (nv && m < kp.M) part[int64_t(m) * kp.N + nrow] = ok ? v[i] : 0.f;
+          if (nv && m < kp.M) part[int64_t(m) * kp.N + n] = ok ? v[i] : 0.f;
         }
       }
     }
   }
 
-  // split-K: the last CTA of this (tile, m-chunk) sums the partials in order
+  // split-K: the last CTA of this (tile, m-chunk) sums the partials in split
+  // order (deterministic)
   if (kp.S > 1) {
     __threadfence();
     __syncthreads();
@@ -356,12 +654,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       const int rows_here = min(kRows, kp.N - n0);
       const int toks = min(kp.MT, kp.M - m0);
-      for (int e = threadIdx.x; e < rows_here * toks; e += blockDim.x) {
-        const int m = m0 + e / rows_here;
-        const int64_t nn = n0 + (e % rows_here);
-        float acc = 0.f;
-        for (int sp = 0; sp < kp.S; ++sp) acc += __ldcg(kp.partials + (int64_t(sp) * kp.M + m) * kp.N + nn);
-        reinterpret_cast<uint16_t*>(kp.c)[int64_t(m) * kp.c_rs + nn] = to16(acc, bf16);
+      const int64_t plane = int64_t(kp.M) * kp.N;
+      uint16_t* c16 = reinterpret_cast<uint16_t*>(kp.c);
+      if ((kp.N & 3) == 0) {
+        // 4 consecutive rows per element, 4 elements per thread in flight
+        const int r4 = rows_here >> 2;
+        const int total = r4 * toks;
+        for (int e0 = threadIdx.x; e0 < total; e0 += kThreads * 4) {
+          float4 acc[4];
+          int64_t off[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = min(e0 + j * kThreads, total - 1);
+            acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            off[j] = int64_t(m0 + e / r4) * kp.N + n0 + 4 * (e % r4);
+          }
+          for (int sp = 0; sp < kp.S; ++sp) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(kp.partials + sp * plane + off[j]));
+              acc[j].x += v.x;
+              acc[j].y += v.y;
+              acc[j].z += v.z;
+              acc[j].w += v.w;
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = e0 + j * kThreads;
+            if (e < total) {
+              const int m = m0 + e / r4;
+              uint16_t* dst = c16 + int64_t(m) * kp.c_rs + n0 + 4 * (e % r4);
+              dst[0] = to16(acc[j].x, bf16);
+              dst[1] = to16(acc[j].y, bf16);
+              dst[2] = to16(acc[j].z, bf16);
+              dst[3] = to16(acc[j].w, bf16);
+            }
+          }
+        }
+      } else {
+        const int total = rows_here * toks;
+        for (int e0 = threadIdx.x; e0 < total; e0 += kThreads * 4) {
+          float acc[4];
+          int64_t off[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = min(e0 + j * kThreads, total - 1);
+            acc[j] = 0.f;
+            off[j] = int64_t(m0 + e / rows_here) * kp.N + n0 + (e % rows_here);
+          }
+          for (int sp = 0; sp < kp.S; ++sp) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] += __ldcg(kp.partials + sp * plane + off[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int e = e0 + j * kThreads;
+            if (e < total) c16[int64_t(m0 + e / rows_here) * kp.c_rs + n0 + (e % rows_here)] = to16(acc[j], bf16);
+          }
+        }
       }
     }
   }
@@ -396,47 +747,98 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.m_chunks = int((M + kMaxMT - 1) / kMaxMT);
   if (p.m_chunks > 1) p.MT = kMaxMT;
   p.tiles_n = int((N + kRows - 1) / kRows);
-  p.nk = int((K + kBK - 1) / kBK);
-  p.n_os = int((n_out + kBK - 1) / kBK);
+  p.nk = int((K + kStep - 1) / kStep);
+  p.ncs = int((K + kCodeK - 1) / kCodeK);
+  p.n_os = int((n_out + kStep - 1) / kStep);
   const int sms = 148;
   const int64_t ctas = int64_t(p.tiles_n) * p.m_chunks;
-  int S = int(std::max<int64_t>(1, (sms + ctas / 2) / ctas));
-  S = std::min(S, std::max(1, p.nk / 4));  // at least 4 stages of work per split
-  p.S = S;
-  const int act_stage = p.MT * 128;
-  p.stages = p.MT >= 192 ? 4 : 6;
-  p.act_stage_bytes = act_stage;
-  p.smem = 1024 + size_t(p.stages) * (act_stage + 4096) + size_t(3 * p.stages + 1) * 8 + 64;
+  p.S = int(std::min<int64_t>(std::max<int64_t>(1, (sms + ctas / 2) / ctas), p.ncs));
+  p.act_stage_bytes = p.MT * 128;
+  p.code_stages = p.MT <= 32 ? 6 : p.MT <= 64 ? 5 : p.MT <= 128 ? 4 : 3;
+  const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 2 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot;
+  const size_t code = size_t(p.code_stages) * (kCodeBytes + 16);
+  p.act_stages = int(std::min<size_t>(kMaxActStages, (kMaxDynSmem - fixed - code) / (p.act_stage_bytes + 16)));
+  p.smem = fixed + code + size_t(p.act_stages) * (p.act_stage_bytes + 16);
+  p.issuers = p.MT <= 32 ? kMaxIssuers : p.MT <= 64 ? 2 : 1;
   p.tmem_cols = 32;
-  while (p.tmem_cols < uint32_t(p.MT + p.stages * 32)) p.tmem_cols <<= 1;
+  while (p.tmem_cols < uint32_t(p.issuers * p.MT + 2 * kCodeK / 2)) p.tmem_cols <<= 1;
   p.workspace = p.S > 1 ? (256 * ((size_t(p.tiles_n) * p.m_chunks * 4 + 255) / 256) + size_t(p.S) * M * N * 4) : 0;
   return p;
 }
 
+namespace {
+
+template <bool BF16, bool SZ_TMA>
+int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmKParams& kp, cudaStream_t st) {
+  auto kern = gemm_w4a16_tc_kernel<BF16, SZ_TMA>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem));
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(pl.tiles_n * pl.S), unsigned(pl.m_chunks));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], kp));
+}
+
+}  // namespace
+
 int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   const GemmPlan pl = plan_gemm(a.M, a.N, a.K, a.n_out);
-  if (pl.tmem_cols > 512 || pl.smem > kMaxDynSmem) return SPECTRA_ERR_UNSUPPORTED;
+  if (pl.tmem_cols > 512 || pl.smem > kMaxDynSmem || pl.act_stages < 3) return SPECTRA_ERR_UNSUPPORTED;
   if (pl.S > 1 && (ws == nullptr || ws_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
   auto enc = encode_fn();
   if (!enc) return SPECTRA_ERR_UNSUPPORTED;
   const bool bf16 = a.a_dtype == SPECTRA_DT_BF16;
+  const int G = a.K / kGroup;
 
-  CUtensorMap mw, ma;
+  CUtensorMap maps[4];  // codes, scales, zero points, activations
+  memset(maps, 0, sizeof(maps));
   {
     cuuint64_t dims[2] = {cuuint64_t(a.K / 2), cuuint64_t(a.N)};
     cuuint64_t strides[1] = {cuuint64_t(a.w_rs)};
-    cuuint32_t box[2] = {32, 128}, es[2] = {1, 1};
-    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.packed), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    cuuint32_t box[2] = {kCodeK / 2, kRows}, es[2] = {1, 1};
+    if (enc(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.packed), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return SPECTRA_ERR_ALIGNMENT;
+  }
+  // scales / zero points by tensor map when their layout allows one (unit
+  // column stride, 16-byte aligned base and row pitch); else by plain loads
+  bool sz_tma = a.s_cs == 1 && a.z_cs == 1 && (a.s_rs * 2) % 16 == 0 && a.z_rs % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(a.scales) % 16 == 0 && reinterpret_cast<uintptr_t>(a.zeros) % 16 == 0 &&
+                sz_tma_enabled();
+  if (sz_tma) {
+    cuuint64_t dims[2] = {cuuint64_t(G), cuuint64_t(a.N)};
+    cuuint64_t s_strides[1] = {cuuint64_t(a.s_rs) * 2};
+    cuuint64_t z_strides[1] = {cuuint64_t(a.z_rs)};
+    cuuint32_t box[2] = {kSzGroups, kRows}, es[2] = {1, 1};
+    sz_tma = enc(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<__half*>(a.scales), dims, s_strides, box,
+                 es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+             enc(&maps[2], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.zeros), dims, z_strides, box, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   }
   {
     cuuint64_t dims[2] = {cuuint64_t(a.K), cuuint64_t(a.M)};
     cuuint64_t strides[1] = {cuuint64_t(a.a_rs) * 2};
-    cuuint32_t box[2] = {64, cuuint32_t(pl.MT)}, es[2] = {1, 1};
-    if (enc(&ma, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.a),
-            dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    cuuint32_t box[2] = {kStep, cuuint32_t(pl.MT)}, es[2] = {1, 1};
+    if (enc(&maps[3], bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+            const_cast<void*>(a.a), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return SPECTRA_ERR_ALIGNMENT;
   }
@@ -449,32 +851,24 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.ow = a.ow; kp.ow_dtype = a.ow_dtype; kp.ow_rs = a.ow_rs; kp.ow_cs = a.ow_cs;
   kp.c = a.c; kp.c_dtype = a.c_dtype; kp.c_rs = a.c_rs;
   kp.M = a.M; kp.N = a.N; kp.K = a.K; kp.layout = a.layout;
-  kp.MT = pl.MT; kp.stages = pl.stages; kp.S = pl.S; kp.nk = pl.nk; kp.n_os = pl.n_os; kp.tiles_n = pl.tiles_n;
+  kp.MT = pl.MT; kp.S = pl.S; kp.nk = pl.nk; kp.ncs = pl.ncs; kp.n_os = pl.n_os; kp.tiles_n = pl.tiles_n;
+  kp.act_stages = pl.act_stages; kp.code_stages = pl.code_stages; kp.issuers = pl.issuers;
   kp.idesc = idesc_f16(bf16, kRows, pl.MT);
   kp.tmem_cols = pl.tmem_cols;
   kp.act_stage_bytes = pl.act_stage_bytes;
+  // shared memory: act slots | code slots | sz slots | barriers (all 1024-aligned
+  // regions: act slots are multiples of 2 KB, code and sz slots of 8 KB)
   kp.off_act = 0;
-  kp.off_w = pl.stages * pl.act_stage_bytes;
-  kp.off_bar = kp.off_w + pl.stages * 4096;
+  kp.off_code = pl.act_stages * pl.act_stage_bytes;
+  kp.off_sz = kp.off_code + pl.code_stages * kCodeBytes;
+  kp.off_bar = kp.off_sz + kSzSlots * kSzSlot;
   if (pl.S > 1) {
     const size_t cnt_bytes = 256 * ((size_t(pl.tiles_n) * pl.m_chunks * 4 + 255) / 256);
     kp.counters = reinterpret_cast<int*>(ws);
     kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + cnt_bytes);
   }
-
-  auto kern = bf16 ? gemm_w4a16_tc_kernel<true> : gemm_w4a16_tc_kernel<false>;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e);
-  if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  static bool attr_set[2][kMaxDevices] = {};
-  if (!attr_set[bf16][dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem));
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[bf16][dev] = true;
-  }
-  kern<<<dim3(unsigned(pl.tiles_n * pl.S), unsigned(pl.m_chunks)), kThreads, pl.smem, st>>>(mw, ma, kp);
-  return cuda_status(cudaGetLastError());
+  if (bf16) return sz_tma ? launch_variant<true, true>(pl, maps, kp, st) : launch_variant<true, false>(pl, maps, kp, st);
+  return sz_tma ? launch_variant<false, true>(pl, maps, kp, st) : launch_variant<false, false>(pl, maps, kp, st);
 }
 
 int gemm_noalloc_scratch(void** ptr, size_t* bytes) {

@@ -11,11 +11,10 @@
 namespace spectra {
 namespace sm100 {
 
-// A bounded wait polls try_wait with a suspend-time hint of kSuspendNs, so a
-// waiting warp sleeps instead of spinning; it gives up after kSpinLimit polls
-// (a few seconds at most).
-constexpr uint32_t kSpinLimit = 1u << 16;
-constexpr uint32_t kSuspendNs = 50000;
+// A bounded wait polls try_wait (no suspend-time hint: a hinted wait was seen
+// to add about a microsecond per pipeline handoff) and gives up once
+// kWaitLimitNs of %globaltimer time have passed, or as soon as `abort` is set.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -44,22 +43,62 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-  }
-  return false;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
+
+// Non-blocking probe of the phase with the given parity (test_wait never
+// suspends the thread, unlike try_wait, whose first call costs ~150 cycles
+// even when the phase has long completed).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  The slow
+// path (and its timer) starts only after the first probe failed.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (*abort) return false;
+      const uint64_t now = global_ns();
+      if (i == 32)
+        t0 = now;
+      else if (now - t0 > kWaitLimitNs)
+        return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  if (mbar_test(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort);
+}
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: wait for the previous grid's memory to be
+// visible / let the next grid start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
