@@ -28,6 +28,7 @@ struct GemmPlan {
   int S;                      // K splits per tile
   int act_stages, code_stages, act_stage_bytes;
   int issuers;                // warps issuing MMAs (each with its own accumulator)
+  int a_slots;                // TMEM A slots of one 256-k unit (2 or 3)
   uint32_t tmem_cols;
   size_t smem, workspace;
 };

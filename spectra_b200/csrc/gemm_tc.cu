@@ -78,6 +78,23 @@ constexpr size_t kMaxDynSmem = 200 * 1024;
 
 __device__ int g_gemm_timeouts;  // stuck pipeline waits since load (diagnostic)
 
+// Position in a ring of `size` slots: slot index and the parity of the pass
+// (the mbarrier phase a consumer of that slot waits for).  Advanced by one per
+// use instead of dividing a running counter by a runtime ring size, which
+// costs a single-thread producer or MMA issuer tens of cycles per division.
+struct Ring {
+  int idx = 0;
+  uint32_t phase = 0;
+  int size;
+  __device__ explicit Ring(int n) : size(n) {}
+  __device__ void next() {
+    if (++idx == size) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 struct GemmKParams {
   const __half* scales; int64_t s_rs, s_cs;
   const uint8_t* zeros; int64_t z_rs, z_cs;
@@ -89,7 +106,7 @@ struct GemmKParams {
   int* counters;    // [tiles_n * m_chunks]
   int M, N, K, layout;
   int MT, S, nk, ncs, n_os, tiles_n;
-  int act_stages, code_stages, issuers;
+  int act_stages, code_stages, issuers, a_slots;
   uint32_t idesc, tmem_cols;
   int off_act, act_stage_bytes, off_code, off_sz, off_bar;
 };
@@ -221,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ GemmKParams kp) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int AS = kp.act_stages, CS = kp.code_stages, NI = kp.issuers;
+  const int AS = kp.act_stages, CS = kp.code_stages, NI = kp.issuers, NAS = kp.a_slots;
   uint8_t* act_st = smem + kp.off_act;     // [AS][MT x 128 B]
   uint8_t* code_st = smem + kp.off_code;   // [CS][128 x 128 B]
   uint8_t* sz_st = smem + kp.off_sz;       // [2][scales 128 x 128 B | zeros 128 x 64 B]
@@ -231,8 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* szfree = szfull + kSzSlots;                               // [2] sz chunk read (8 warps)
   uint64_t* afull = szfree + kSzSlots;                                // [AS] act slot landed / filled
   uint64_t* afree = afull + AS;                                       // [AS] act slot consumed by MMAs
-  uint64_t* aready = afree + AS;                                      // [2] A slot written (8 warps)
-  uint64_t* mdone = aready + 2;                                       // [kDone] unit's MMAs complete (NI)
+  uint64_t* aready = afree + AS;                                      // [NAS] A slot written (8 warps)
+  uint64_t* mdone = aready + NAS;                                     // [kDone] unit's MMAs complete (NI)
   uint64_t* accf = mdone + kDone;                                     // accumulators final (NI)
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -286,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(afull + i, 1);
       mbar_init(afree + i, NI);  // one commit per MMA issuer
     }
-    for (int i = 0; i < 2; ++i) mbar_init(aready + i, kDeqWarps);
+    for (int i = 0; i < NAS; ++i) mbar_init(aready + i, kDeqWarps);
     for (int i = 0; i < kDone; ++i) mbar_init(mdone + i, NI);  // one commit per MMA issuer
     mbar_init(accf, NI);
     fence_mbar_init();
@@ -301,8 +318,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
 
-  // weight producer (warp 0, lane 0): code stage lc -> slot lc % CS, preceded by
-  // its sz chunk when lc starts one.  Returns false if a wait gave up.
+  // weight producer (warp 0, lane 0): code stage lc -> slot ring.idx, preceded
+  // by its sz chunk when lc starts one.  Returns false if a wait gave up.
+  Ring wring(CS);
   auto issue_weights = [&](int lc, bool may_wait) -> bool {
     if constexpr (SZ_TMA) {
       const int ch = sz_of(lc);
@@ -316,9 +334,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(slot + kSzScaleBytes, &map_z, (sz0 + ch) * kSzGroups, n0, bar);
       }
     }
-    if (lc >= CS && !(may_wait && mbar_wait(cfree + lc % CS, uint32_t((lc / CS - 1) & 1), &s_abort))) return false;
-    mbar_arrive_expect_tx(cfull + lc % CS, uint32_t(kCodeBytes));
-    tma_load_2d(code_st + (lc % CS) * kCodeBytes, &map_w, (cs0 + lc) * (kCodeK / 2), n0, cfull + lc % CS);
+    const int c = wring.idx;
+    if (lc >= CS && !(may_wait && mbar_wait(cfree + c, wring.phase ^ 1u, &s_abort))) return false;
+    mbar_arrive_expect_tx(cfull + c, uint32_t(kCodeBytes));
+    tma_load_2d(code_st + c * kCodeBytes, &map_w, (cs0 + lc) * (kCodeK / 2), n0, cfull + c);
+    wring.next();
     return true;
   };
   // The packed codes, scales and zero points are constant weights, never
@@ -340,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   pdl_trigger();
   const uint32_t tmem = s_tmem;
-  // TMEM columns: one fp32 accumulator [128 x MT] per MMA issuer, then two A
-  // slots of 128 columns (one unit = 4 steps x 32 columns each)
+  // TMEM columns: one fp32 accumulator [128 x MT] per MMA issuer, then NAS
+  // (2 or 3) A slots of 128 columns (one unit = 4 steps x 32 columns each)
   const uint32_t a_col0 = uint32_t(NI * kp.MT);
   const bool bf16 = BF16;
   const int zero_flag = 0;
@@ -362,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // every TMA copy issued must land before the CTA may exit (bounded wait,
       // ignoring the abort flag); on the normal path these completed long ago
       for (int lc = max(0, issued - CS); lc < issued; ++lc)
-        mbar_wait(cfull + lc % CS, uint32_t((lc / CS) & 1), &zero_flag);
+        mbar_wait(cfull + lc % CS, uint32_t((lc / CS) & 1), &zero_flag);  // once, at exit
       if constexpr (SZ_TMA) {
         if (issued > 0) {
           const int last = sz_of(issued - 1);
@@ -377,9 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // may have more steps than there are slots)
     if (lane == 0) {
       int issued = 0;
-      for (int st = 0; st < n_it; ++st) {
-        const int sa = st % AS;
-        if (st >= AS && !mbar_wait(afree + sa, uint32_t((st / AS - 1) & 1), &s_abort)) {
+      Ring ar(AS);
+      for (int st = 0; st < n_it; ++st, ar.next()) {
+        const int sa = ar.idx;
+        if (st >= AS && !mbar_wait(afree + sa, ar.phase ^ 1u, &s_abort)) {
           s_abort = 1;
           atomicAdd(&g_gemm_timeouts, 1);
           break;
@@ -393,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = st + 1;
       }
       for (int st = max(0, issued - AS); st < issued; ++st)
-        mbar_wait(afull + st % AS, uint32_t((st / AS) & 1), &zero_flag);
+        mbar_wait(afull + st % AS, uint32_t((st / AS) & 1), &zero_flag);  // once, at exit
     }
   } else if (warp == 1 || warp > kActWarp) {
     // ---------------------------------------------------------------- MMA issue
@@ -406,32 +427,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (issuer < NI && lane == 0) {
       const uint32_t d_tmem = tmem + uint32_t(issuer * kp.MT);
       bool live = true;
-      for (int u = 0; u < n_units && live; ++u) {
+      Ring ar(AS), asl(NAS);
+      for (int u = 0; u < n_units && live; ++u, asl.next()) {
         const int ns = steps_of(u);
-        if (!mbar_wait(aready + (u & 1), uint32_t((u >> 1) & 1), &s_abort)) {
+        if (!mbar_wait(aready + asl.idx, asl.phase, &s_abort)) {
           s_abort = 1;
           atomicAdd(&g_gemm_timeouts, 1);
           live = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_unit = tmem + a_col0 + uint32_t((u & 1) * 128);
-        for (int j = 0; j < ns && live; ++j) {
-          const int st = step_of(u, j);
-          if (!mbar_wait(afull + st % AS, uint32_t((st / AS) & 1), &s_abort)) {
+        const uint32_t a_unit = tmem + a_col0 + uint32_t(asl.idx * 128);
+        for (int j = 0; j < ns && live; ++j, ar.next()) {
+          if (!mbar_wait(afull + ar.idx, ar.phase, &s_abort)) {
             s_abort = 1;
             atomicAdd(&g_gemm_timeouts, 1);
             live = false;
             break;
           }
           tc_fence_after();
-          const uint32_t b_base = smem_u32(act_slot(u, j));
+          const uint32_t b_base = smem_u32(act_st + ar.idx * act_bytes);
           for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
             const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
             mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
                    (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
           }
-          mma_commit(afree + st % AS);
+          mma_commit(afree + ar.idx);
         }
         if (!live) break;
         mma_commit(mdone + u % kDone);
@@ -459,11 +480,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       return ok;
     };
     // this unit's A slot written: hand it to the MMA issuers
-    auto publish = [&](int u) {
+    Ring asl(NAS);
+    auto publish = [&]() {
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(aready + (u & 1));
+      if (lane == 0) mbar_arrive(aready + asl.idx);
+      asl.next();
     };
 
     // scale / zero point of this row for the four groups 2j+h of code stage lc
@@ -487,15 +510,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool alive = true;
     auto main_units = [&](auto marlin_tag) {
       constexpr bool kMarlin = decltype(marlin_tag)::value;
-      for (int lc = 0; lc < n_code && alive; ++lc) {
-        const int c = lc % CS;
+      Ring cr(CS);
+      for (int lc = 0; lc < n_code && alive; ++lc, cr.next()) {
+        const int c = cr.idx;
         const uint8_t* slot = code_st + c * kCodeBytes;
         const int ch = sz_of(lc);
         const bool first_of_sz = (lc == 0 || ch != sz_of(lc - 1));
         const bool last_of_sz = (lc == n_code - 1 || ch != sz_of(lc + 1));
-        // A slot free (MMAs of unit lc - 2 done), codes and sz landed
-        if ((lc >= 2 && !wait_all(mdone + (lc - 2) % kDone, done_parity(lc - 2))) ||
-            !wait_all(cfull + c, uint32_t((lc / CS) & 1)) ||
+        // A slot free (MMAs of unit lc - NAS done), codes and sz landed
+        if ((lc >= NAS && !wait_all(mdone + (lc - NAS) % kDone, done_parity(lc - NAS))) ||
+            !wait_all(cfull + c, cr.phase) ||
             (SZ_TMA && first_of_sz && !wait_all(szfull + ch % kSzSlots, uint32_t((ch / kSzSlots) & 1)))) {
           alive = false;
           break;
@@ -531,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           load_sz(lc + 1, s_next, z_next);
         }
-        const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t((lc & 1) * 128);
+        const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t(asl.idx * 128);
         const int ns = steps_of(lc);
 #pragma unroll
         for (int j = 0; j < kStepsPerCode; ++j) {
@@ -546,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
           }
         }
-        publish(lc);
+        publish();
         // this code stage has been read: hand the slot back to the producer
         if (lane == 0) mbar_arrive(cfree + c);
       }
@@ -558,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // outlier units: columns j0 .. j0+63 of ow / of a[:, idx] per step
     for (int u = n_code; u < n_units && alive; ++u) {
-      bool ok = u < 2 || wait_all(mdone + (u - 2) % kDone, done_parity(u - 2));
+      bool ok = u < NAS || wait_all(mdone + (u - NAS) % kDone, done_parity(u - NAS));
       const int ns = steps_of(u);
       for (int j = 0; j < ns && ok; ++j) {
         const int st = step_of(u, j);
@@ -566,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       tc_fence_after();
-      const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t((u & 1) * 128);
+      const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t(asl.idx * 128);
       for (int j = 0; j < ns; ++j) {
         const int j0 = (step_of(u, j) - n_main) * kStep;
         uint32_t vals[16];
@@ -595,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
       }
       fence_proxy_async_smem();
-      publish(u);
+      publish();
     }
 
     // ---------------------------------------------------------------- epilogue
@@ -755,13 +779,15 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.S = int(std::min<int64_t>(std::max<int64_t>(1, (sms + ctas / 2) / ctas), p.ncs));
   p.act_stage_bytes = p.MT * 128;
   p.code_stages = p.MT <= 32 ? 6 : p.MT <= 64 ? 5 : p.MT <= 128 ? 4 : 3;
-  const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 2 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot;
+  const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 3 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot;
   const size_t code = size_t(p.code_stages) * (kCodeBytes + 16);
   p.act_stages = int(std::min<size_t>(kMaxActStages, (kMaxDynSmem - fixed - code) / (p.act_stage_bytes + 16)));
   p.smem = fixed + code + size_t(p.act_stages) * (p.act_stage_bytes + 16);
   p.issuers = p.MT <= 32 ? kMaxIssuers : p.MT <= 64 ? 2 : 1;
+  // a third A slot (128 columns) where the accumulators leave room for it
+  p.a_slots = p.issuers * p.MT + 3 * 128 <= 512 ? 3 : 2;
   p.tmem_cols = 32;
-  while (p.tmem_cols < uint32_t(p.issuers * p.MT + 2 * kCodeK / 2)) p.tmem_cols <<= 1;
+  while (p.tmem_cols < uint32_t(p.issuers * p.MT + p.a_slots * 128)) p.tmem_cols <<= 1;
   p.workspace = p.S > 1 ? (256 * ((size_t(p.tiles_n) * p.m_chunks * 4 + 255) / 256) + size_t(p.S) * M * N * 4) : 0;
   return p;
 }
@@ -853,6 +879,7 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.M = a.M; kp.N = a.N; kp.K = a.K; kp.layout = a.layout;
   kp.MT = pl.MT; kp.S = pl.S; kp.nk = pl.nk; kp.ncs = pl.ncs; kp.n_os = pl.n_os; kp.tiles_n = pl.tiles_n;
   kp.act_stages = pl.act_stages; kp.code_stages = pl.code_stages; kp.issuers = pl.issuers;
+  kp.a_slots = pl.a_slots;
   kp.idesc = idesc_f16(bf16, kRows, pl.MT);
   kp.tmem_cols = pl.tmem_cols;
   kp.act_stage_bytes = pl.act_stage_bytes;
