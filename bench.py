@@ -16,6 +16,11 @@ random N(0, 0.02) fp16 quantised on the device by ``spectra_b200.compress``
           the step's activations copied from pinned host memory and all seven
           outputs copied back, every step, inside the timed region.
 
+The line also carries ``gemm_sweep``: the M >= 2 tensor-core
+GEMM ``batched_w4a16_gemm`` on the Llama-3-8B linear shapes (K x N) 4096x4096,
+4096x1024, 4096x14336, 14336x4096 at M = 16, 64, 256 (TFLOP/s), and the M = 1
+GEMV on the same shapes (GB/s), weights rotated over copies totalling > 3 x L2.
+
 ``--impl reference`` times the reference's CPU formula for the same layer
 (``oracle/cpu_path.py``) on the host cores instead.  Under torchrun (N>1) every
 rank runs the same single-GPU workload on its own layer copies (replicas:
@@ -220,6 +225,52 @@ def time_events(fn, dev) -> float:
     return a.elapsed_time(b) / 1e3
 
 
+GEMM_SHAPES = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]  # (K, N)
+GEMM_MS = (16, 64, 256)
+
+
+def gemm_sweep(SK, dev) -> dict:
+    """BASELINE config 3 on one GPU: per shape, one matrix quantised on the device
+    (N(0, 0.02) fp16 weights, SPECTRA format, Marlin order) cloned into enough
+    copies to exceed 3 x L2; each point is the mean of graph replays over the
+    copies, CUDA events on the launching stream."""
+    from spectra_b200 import compress as C
+    res = []
+    for K, N in GEMM_SHAPES:
+        g = torch.Generator(device=dev).manual_seed(K * 7 + N)
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.float16)
+        c = C.compress_linear(w)
+        del w
+        wbytes = algorithmic_bytes(0, N, K, c.outlier_idx.numel())
+        copies = max(2, min(32, int(3 * 126e6 // wbytes) + 1))
+        mats = [(c.packed.clone(), c.scales.clone(), c.zeros.clone(), c.outlier_idx, c.outlier_w.clone())
+                for _ in range(copies)]
+        for M in (1,) + GEMM_MS:
+            a = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            outs = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(copies)]
+
+            def run_all():
+                for (p, s_, z, idx, ow), o in zip(mats, outs):
+                    if M == 1:
+                        SK.fused_w4a16_gemv_hdsq(a, p, s_, z, outlier_idx=idx, outlier_w=ow, out=o, marlin_layout=True)
+                    else:
+                        SK.batched_w4a16_gemm(a, p, s_, z, outlier_idx=idx, outlier_w=ow, marlin_layout=True)
+            gr = capture(run_all, dev)
+            for _ in range(3):
+                gr.replay()
+            reps = 10
+            dt = time_events(lambda: [gr.replay() for _ in range(reps)], dev) / (reps * copies)
+            byts = algorithmic_bytes(M, N, K, c.outlier_idx.numel())
+            r = {"K": K, "N": N, "M": M, "us": round(dt * 1e6, 2), "gbs": round(byts / dt / 1e9, 1)}
+            if M > 1:
+                r["tflops"] = round(2.0 * M * N * (K + c.outlier_idx.numel()) / dt / 1e12, 2)
+            res.append(r)
+            del gr
+        del mats
+    return {"unit": "TFLOP/s (M >= 2), GB/s (M = 1)", "results": res,
+            "note": "TFLOP/s counts 2*M*N*(K + outlier columns); GB/s counts the algorithmic bytes"}
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -392,6 +443,8 @@ def run_gpu(args, world, rank, local):
     dt_e2e = max_over_ranks(dt_e2e, world, dev)
     e2e_value = bytes_step * args.steps * world / dt_e2e / 1e9
 
+    sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
+
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
     if rank == 0:
@@ -415,6 +468,7 @@ def run_gpu(args, world, rank, local):
                          "avg_launch_us": round(dt_gate * 1e6, 3)},
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": cpu,
+            "gemm_sweep": sweep,
         }
         print(json.dumps(line), flush=True)
     for g in singles + [cycle, g_gate]:
@@ -428,6 +482,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
+    ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the config-3 GEMM/GEMV shape sweep")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
