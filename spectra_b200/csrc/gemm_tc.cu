@@ -108,7 +108,7 @@ struct GemmKParams {
   int MT, S, nk, ncs, n_os, tiles_n;
   int act_stages, code_stages, issuers, a_slots;
   uint32_t idesc, tmem_cols;
-  int off_act, act_stage_bytes, off_code, off_sz, off_bar;
+  int off_act, act_stage_bytes, off_code, off_sz, off_oidx, off_bar;
 };
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* act_st = smem + kp.off_act;     // [AS][MT x 128 B]
   uint8_t* code_st = smem + kp.off_code;   // [CS][128 x 128 B]
   uint8_t* sz_st = smem + kp.off_sz;       // [2][scales 128 x 128 B | zeros 128 x 64 B]
+  int* oidx = reinterpret_cast<int*>(smem + kp.off_oidx);  // [n_os * 64] outlier columns (-1: none)
   uint64_t* cfull = reinterpret_cast<uint64_t*>(smem + kp.off_bar);  // [CS] code stage landed
   uint64_t* cfree = cfull + CS;                                       // [CS] code stage read (8 warps)
   uint64_t* szfull = cfree + CS;                                      // [2] sz chunk landed
@@ -272,17 +273,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_code = cs1 - cs0;
   const int st0 = cs0 * kStepsPerCode;
   const int n_main = min(kp.nk, cs1 * kStepsPerCode) - st0;
-  const int n_out_st = (split == kp.S - 1) ? kp.n_os : 0;
+  // outlier steps dealt round-robin over the K splits (split s: steps s, s+S, ...)
+  const int n_out_st = kp.n_os > split ? (kp.n_os - split + kp.S - 1) / kp.S : 0;
+  auto ostep = [&](int local) { return split + kp.S * local; };  // global outlier step
   const int n_it = n_main + n_out_st;
-  const int n_units = n_code + (n_out_st + kStepsPerCode - 1) / kStepsPerCode;
+  // Outlier units come first: their loads (outlier weights, gathered
+  // activations) then overlap the arrival of the first code stages instead of
+  // extending the end of the pipeline.  Units [0, n_ou) are outlier steps,
+  // units [n_ou, n_units) the code stages.
+  const int n_ou = (n_out_st + kStepsPerCode - 1) / kStepsPerCode;
+  const int n_units = n_ou + n_code;
   auto steps_of = [&](int u) {
-    return u < n_code ? min(kStepsPerCode, n_main - u * kStepsPerCode)
-                      : min(kStepsPerCode, n_out_st - (u - n_code) * kStepsPerCode);
+    return u < n_ou ? min(kStepsPerCode, n_out_st - u * kStepsPerCode)
+                    : min(kStepsPerCode, n_main - (u - n_ou) * kStepsPerCode);
   };
+  // steps in unit order: n_out_st outlier steps (last outlier unit may be
+  // short), then the main steps
   auto step_of = [&](int u, int j) {
-    return u < n_code ? u * kStepsPerCode + j : n_main + (u - n_code) * kStepsPerCode + j;
+    return u < n_ou ? u * kStepsPerCode + j : n_out_st + (u - n_ou) * kStepsPerCode + j;
   };
-  auto unit_of = [&](int st) { return st < n_main ? st / kStepsPerCode : n_code + (st - n_main) / kStepsPerCode; };
   const uint32_t act_bytes = uint32_t(kp.act_stage_bytes);
   auto act_slot = [&](int u, int j) -> uint8_t* { return act_st + (step_of(u, j) % AS) * act_bytes; };
   // sz chunk (local index) of local code stage lc
@@ -405,9 +414,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           atomicAdd(&g_gemm_timeouts, 1);
           break;
         }
-        if (st < n_main) {
+        if (st >= n_out_st) {
           mbar_arrive_expect_tx(afull + sa, act_bytes);
-          tma_load_2d(act_st + sa * act_bytes, &map_a, (st0 + st) * kStep, m0, afull + sa);
+          tma_load_2d(act_st + sa * act_bytes, &map_a, (st0 + st - n_out_st) * kStep, m0, afull + sa);
         } else {
           mbar_arrive(afull + sa);  // outlier step: the dequant warps fill the slot
         }
@@ -507,7 +516,93 @@ __global__ void __launch_bounds__(kThreads, 1)
     float s_next[4], z_next[4];
     if constexpr (!SZ_TMA) load_sz(0, s_next, z_next);
 
+    // outlier column indices of this CTA's outlier steps, once (the gather of
+    // a[:, idx] then needs a single dependent load per element)
+    if (n_out_st > 0) {
+      const int tid_d = (warp - 2) * 32 + lane;
+      for (int j = tid_d; j < n_out_st * kStep; j += kDeqWarps * 32) {
+        const int jg = ostep(j / kStep) * kStep + j % kStep;  // outlier column
+        int64_t k = jg < kp.n_out ? load_index(kp.idx, jg, kp.idx_dtype) : -1;
+        oidx[j] = (k >= 0 && k < kp.K) ? int(k) : -1;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kDeqWarps * 32) : "memory");  // dequant warps only
+    }
+
     bool alive = true;
+    // outlier units: columns j0 .. j0+63 of ow / of a[:, idx] per step
+    for (int u = 0; u < n_ou && alive; ++u) {
+      bool ok = u < NAS || wait_all(mdone + (u - NAS) % kDone, done_parity(u - NAS));
+      const int ns = steps_of(u);
+      for (int j = 0; j < ns && ok; ++j) {
+        const int st = step_of(u, j);
+        ok = wait_all(afull + st % AS, uint32_t((st / AS) & 1));
+      }
+      if (!ok) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t(asl.idx * 128);
+      for (int j = 0; j < ns; ++j) {
+        const int jl = step_of(u, j);       // local outlier step
+        const int j0 = ostep(jl) * kStep;   // its first outlier column
+        // this row's 32 outlier weights of the step, 16 at a time: the dtype is
+        // resolved once, then the loads go out back to back (predicated)
+        uint32_t vals[16];
+        const int64_t obase = n * kp.ow_rs;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int jb = j0 + h * 32 + half * 16;
+          float ov[16];
+          if (kp.ow_dtype == SPECTRA_DT_F32) {
+            const float* o32 = reinterpret_cast<const float*>(kp.ow);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              ov[i] = (nv && jb + i < kp.n_out) ? __ldg(o32 + obase + int64_t(jb + i) * kp.ow_cs) : 0.f;
+          } else {
+            const unsigned short* o16 = reinterpret_cast<const unsigned short*>(kp.ow);
+            unsigned short raw[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              raw[i] = (nv && jb + i < kp.n_out) ? __ldg(o16 + obase + int64_t(jb + i) * kp.ow_cs) : (unsigned short)0;
+            const bool obf = kp.ow_dtype == SPECTRA_DT_BF16;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              ov[i] = obf ? __uint_as_float(uint32_t(raw[i]) << 16) : __half2float(__ushort_as_half(raw[i]));
+          }
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) vals[half * 8 + cc] = pack2<BF16>(ov[2 * cc], ov[2 * cc + 1]);
+        }
+        // gather a[m0+m, idx[j0+jj]] into the act slot, 128B-swizzled K-major;
+        // 8 independent loads in flight per thread
+        uint8_t* bst = act_slot(u, j);
+        const int tid_d = (warp - 2) * 32 + lane;
+        constexpr int kBatch = 8;
+        for (int e0 = tid_d; e0 < kp.MT * kStep; e0 += kDeqWarps * 32 * kBatch) {
+          uint16_t v[kBatch];
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            const int e = e0 + i * kDeqWarps * 32;
+            const int m = e / kStep, jj = e % kStep;
+            const int k = e < kp.MT * kStep ? oidx[jl * kStep + jj] : -1;
+            v[i] = (k >= 0 && m0 + m < kp.M) ? load_act16(kp.a, int64_t(m0 + m) * kp.a_rs + k) : uint16_t(0);
+          }
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) {
+            const int e = e0 + i * kDeqWarps * 32;
+            if (e < kp.MT * kStep) {
+              const int m = e / kStep, jj = e % kStep;
+              const int chunk = (jj >> 3) ^ (m & 7);
+              *reinterpret_cast<uint16_t*>(bst + m * 128 + chunk * 16 + (jj & 7) * 2) = v[i];
+            }
+          }
+        }
+        tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
+      }
+      fence_proxy_async_smem();
+      publish();
+    }
+
     auto main_units = [&](auto marlin_tag) {
       constexpr bool kMarlin = decltype(marlin_tag)::value;
       Ring cr(CS);
@@ -517,8 +612,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ch = sz_of(lc);
         const bool first_of_sz = (lc == 0 || ch != sz_of(lc - 1));
         const bool last_of_sz = (lc == n_code - 1 || ch != sz_of(lc + 1));
-        // A slot free (MMAs of unit lc - NAS done), codes and sz landed
-        if ((lc >= NAS && !wait_all(mdone + (lc - NAS) % kDone, done_parity(lc - NAS))) ||
+        // A slot free (MMAs of unit u - NAS done), codes and sz landed
+        const int u = n_ou + lc;
+        if ((u >= NAS && !wait_all(mdone + (u - NAS) % kDone, done_parity(u - NAS))) ||
             !wait_all(cfull + c, cr.phase) ||
             (SZ_TMA && first_of_sz && !wait_all(szfull + ch % kSzSlots, uint32_t((ch / kSzSlots) & 1)))) {
           alive = false;
@@ -556,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           load_sz(lc + 1, s_next, z_next);
         }
         const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t(asl.idx * 128);
-        const int ns = steps_of(lc);
+        const int ns = steps_of(u);
 #pragma unroll
         for (int j = 0; j < kStepsPerCode; ++j) {
           if (j < ns) {  // K tail (warp-uniform)
@@ -579,48 +675,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       main_units(std::true_type{});
     else
       main_units(std::false_type{});
-
-    // outlier units: columns j0 .. j0+63 of ow / of a[:, idx] per step
-    for (int u = n_code; u < n_units && alive; ++u) {
-      bool ok = u < NAS || wait_all(mdone + (u - NAS) % kDone, done_parity(u - NAS));
-      const int ns = steps_of(u);
-      for (int j = 0; j < ns && ok; ++j) {
-        const int st = step_of(u, j);
-        ok = wait_all(afull + st % AS, uint32_t((st / AS) & 1));
-      }
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t a_unit = tmem + lane_base + a_col0 + uint32_t(asl.idx * 128);
-      for (int j = 0; j < ns; ++j) {
-        const int j0 = (step_of(u, j) - n_main) * kStep;
-        uint32_t vals[16];
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          float lo = 0.f, hi = 0.f;
-          const int jo = j0 + h * 32 + 2 * cc;
-          if (nv && jo < kp.n_out) lo = load_as_float(kp.ow, n * kp.ow_rs + int64_t(jo) * kp.ow_cs, kp.ow_dtype);
-          if (nv && jo + 1 < kp.n_out) hi = load_as_float(kp.ow, n * kp.ow_rs + int64_t(jo + 1) * kp.ow_cs, kp.ow_dtype);
-          vals[cc] = pack2<BF16>(lo, hi);
-        }
-        // gather a[m0+m, idx[j0+jj]] into the act slot, 128B-swizzled K-major
-        uint8_t* bst = act_slot(u, j);
-        const int tid_d = (warp - 2) * 32 + lane;
-        for (int e = tid_d; e < kp.MT * kStep; e += kDeqWarps * 32) {
-          const int m = e / kStep, jj = e % kStep;
-          uint16_t v = 0;
-          const int jo = j0 + jj;
-          if (m0 + m < kp.M && jo < kp.n_out) {
-            const int64_t k = load_index(kp.idx, jo, kp.idx_dtype);
-            if (k >= 0 && k < kp.K) v = load_act16(kp.a, int64_t(m0 + m) * kp.a_rs + k);
-          }
-          const int chunk = (jj >> 3) ^ (m & 7);
-          *reinterpret_cast<uint16_t*>(bst + m * 128 + chunk * 16 + (jj & 7) * 2) = v;
-        }
-        tmem_st_x16(a_unit + uint32_t(j * 32 + h * 16), vals);
-      }
-      fence_proxy_async_smem();
-      publish();
-    }
 
     // ---------------------------------------------------------------- epilogue
     // n_it == 0 cannot happen (S <= ncs), but an empty split would leave the
@@ -779,7 +833,8 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.S = int(std::min<int64_t>(std::max<int64_t>(1, (sms + ctas / 2) / ctas), p.ncs));
   p.act_stage_bytes = p.MT * 128;
   p.code_stages = p.MT <= 32 ? 6 : p.MT <= 64 ? 5 : p.MT <= 128 ? 4 : 3;
-  const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 3 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot;
+  const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 3 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot +
+                       size_t(p.n_os) * kStep * 4;  // + outlier column indices
   const size_t code = size_t(p.code_stages) * (kCodeBytes + 16);
   p.act_stages = int(std::min<size_t>(kMaxActStages, (kMaxDynSmem - fixed - code) / (p.act_stage_bytes + 16)));
   p.smem = fixed + code + size_t(p.act_stages) * (p.act_stage_bytes + 16);
@@ -888,7 +943,8 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.off_act = 0;
   kp.off_code = pl.act_stages * pl.act_stage_bytes;
   kp.off_sz = kp.off_code + pl.code_stages * kCodeBytes;
-  kp.off_bar = kp.off_sz + kSzSlots * kSzSlot;
+  kp.off_oidx = kp.off_sz + kSzSlots * kSzSlot;
+  kp.off_bar = kp.off_oidx + pl.n_os * kStep * 4;
   if (pl.S > 1) {
     const size_t cnt_bytes = 256 * ((size_t(pl.tiles_n) * pl.m_chunks * 4 + 255) / 256);
     kp.counters = reinterpret_cast<int*>(ws);

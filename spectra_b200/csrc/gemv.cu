@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "gemv.h"
 #include "sm100_ptx.cuh"
+#include "gemv_mma.cuh"
 
 namespace spectra {
 
@@ -537,45 +538,6 @@ int launch_rows_align(const GemvKParams& kp, const GemvPlan& pl, cudaStream_t st
 // round-robin to its warps and each unit's partial row sums go to shared
 // memory, summed in a fixed order at the end (deterministic).
 // ---------------------------------------------------------------------------
-template <bool BF16>
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  if constexpr (BF16) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-}
-
-// Pair type t of a 32-bit code word (bytes b0..b3): t=0 {b0.lo, b2.lo},
-// t=1 {b0.hi, b2.hi}, t=2 {b1.lo, b3.lo}, t=3 {b1.hi, b3.hi}.  One shift
-// brings the pair's nibbles to the top four mantissa bits of each 16-bit
-// half, one LOP3 masks them and ORs in the exponent of 16.0: each half is
-// then exactly 16 + q (bf16: nibble at bits 3-6; fp16: bits 6-9).  The small
-// offset keeps the fp32 accumulation of (16 + q) * x as accurate as q * x.
-template <bool BF16, int T>
-__device__ __forceinline__ uint32_t pair_code(uint32_t w, uint32_t magic_reg) {
-  constexpr int kShift = BF16 ? 3 - 4 * T : 6 - 4 * T;  // > 0: left shift
-  constexpr uint32_t kMask = BF16 ? 0x00780078u : 0x03C003C0u;
-  const uint32_t v = kShift >= 0 ? (w << (kShift >= 0 ? kShift : 0)) : (w >> (kShift < 0 ? -kShift : 0));
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "n"(kMask), "r"(magic_reg));
-  return r;
-}
-
-// k (0..31, within the group) of the low / high code of pair kk = 4j + t.
-__host__ __device__ __forceinline__ int pair_k(int kk, int high, int layout) {
-  const int j = kk >> 2, t = kk & 3;
-  const int byte = 4 * j + 2 * high + (t >> 1);
-  return code_k(byte, t & 1, layout);
-}
-
 struct MmaUnitRegs {
   uint4 w[4];     // codes: [grpA row g, grpA row g+8, grpB row g, grpB row g+8]
   uint32_t s[2];  // scales (fp16 pairs {grpA, grpB}) of rows g, g+8
