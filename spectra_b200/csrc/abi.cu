@@ -48,6 +48,14 @@ bool mma_path_enabled() {
   return on;
 }
 
+bool pf_path_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SPECTRA_B200_GEMV_PF");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 bool sz_tma_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("SPECTRA_B200_GEMM_SZ_TMA");

@@ -28,6 +28,10 @@ bool pdl_enabled();
 // SPECTRA_B200_GEMV_MMA=0, which selects the exact CUDA-core kernel).
 bool mma_path_enabled();
 
+// M=1 GEMV weight-prefetching kernel for layouts that allow it (on unless
+// SPECTRA_B200_GEMV_PF=0).
+bool pf_path_enabled();
+
 // GEMM scales / zero points fetched by tensor map when their layout allows
 // (on unless SPECTRA_B200_GEMM_SZ_TMA=0, which forces the plain-load path).
 bool sz_tma_enabled();
@@ -52,6 +56,30 @@ __device__ __forceinline__ float load_as_float(const void* base, int64_t i, int 
     return __half2float(__ldg(reinterpret_cast<const __half*>(base) + i));
   }
   return __ldg(reinterpret_cast<const float*>(base) + i);
+}
+
+// Same, through L2 only (ld.global.cg): for data another kernel may have
+// written while this one was already resident.
+__device__ __forceinline__ float load_as_float_cg(const void* base, int64_t i, int dt) {
+  if (dt == SPECTRA_DT_BF16) {
+    uint16_t b = __ldcg(reinterpret_cast<const unsigned short*>(base) + i);
+    return __uint_as_float(uint32_t(b) << 16);
+  }
+  if (dt == SPECTRA_DT_F16) {
+    return __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(base) + i)));
+  }
+  return __ldcg(reinterpret_cast<const float*>(base) + i);
+}
+
+// Raw bits of one element (through L2 only) and their later conversion.
+__device__ __forceinline__ uint32_t load_bits_cg(const void* base, int64_t i, int dt) {
+  if (dt == SPECTRA_DT_BF16 || dt == SPECTRA_DT_F16) return __ldcg(reinterpret_cast<const unsigned short*>(base) + i);
+  return __ldcg(reinterpret_cast<const unsigned int*>(base) + i);
+}
+__device__ __forceinline__ float bits_to_float(uint32_t b, int dt) {
+  if (dt == SPECTRA_DT_BF16) return __uint_as_float(b << 16);
+  if (dt == SPECTRA_DT_F16) return __half2float(__ushort_as_half(uint16_t(b)));
+  return __uint_as_float(b);
 }
 
 __device__ __forceinline__ int64_t load_index(const void* base, int64_t i, int dt) {

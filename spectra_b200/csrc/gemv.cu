@@ -90,36 +90,6 @@ __device__ __forceinline__ float group_qdot(const uint4 w, const float2 (&xr)[16
   return t.x + t.y;
 }
 
-template <int R>
-__device__ __forceinline__ void warp_transpose_reduce(float (&v)[R], int lane) {
-  // Each stage halves the rows a lane holds: the lower half-warp keeps the
-  // first half of its rows, the upper half keeps the second half.
-  int off = 16;
-#pragma unroll
-  for (int half = R / 2; half >= 1; half /= 2) {
-    const bool up = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const float send = up ? v[i] : v[i + half];
-      const float keep = up ? v[i + half] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-    off >>= 1;
-  }
-  for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
-}
-
-template <int R>
-__device__ __forceinline__ int reduced_row(int lane) {
-  int row = 0, off = 16;
-#pragma unroll
-  for (int half = R / 2; half >= 1; half /= 2) {
-    if (lane & off) row += half;
-    off >>= 1;
-  }
-  return row;
-}
-
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -219,25 +189,7 @@ __device__ __forceinline__ void stage_x_window(const GemvArgs& p, bool vec_x, fl
     }
 }
 
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
-               : "memory");
-}
-
 __device__ int g_gemv_timeouts;  // stuck pipeline waits since load (diagnostic)
-
-inline int device_sms(int dev) {
-  static int sms[kMaxDevices] = {};
-  if (dev < 0 || dev >= kMaxDevices) return 148;
-  if (sms[dev] == 0) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-    sms[dev] = v;
-  }
-  return sms[dev];
-}
 
 // ---------------------------------------------------------------------------
 // Rows kernel (main path).
@@ -893,6 +845,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   // bf16 / fp16 activations: tensor-core kernel; fp32 activations keep the
   // exact CUDA-core kernel (an fp32 x cannot be an MMA operand unrounded).
   if (mma_path_enabled() && (a.x_dtype == SPECTRA_DT_BF16 || a.x_dtype == SPECTRA_DT_F16)) {
+    const int r = launch_gemv_pf(a, st);
+    if (r != SPECTRA_ERR_UNSUPPORTED) return r;
     const bool bf = a.x_dtype == SPECTRA_DT_BF16;
     if (align == 16) return bf ? launch_mma<true, 16>(kp, pl, st) : launch_mma<false, 16>(kp, pl, st);
     if (align == 4) return bf ? launch_mma<true, 4>(kp, pl, st) : launch_mma<false, 4>(kp, pl, st);

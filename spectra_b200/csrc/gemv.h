@@ -35,6 +35,10 @@ struct GemvPlan {
 GemvPlan plan_gemv(int64_t N, int64_t K, int64_t n_out);
 int launch_gemv(const GemvArgs& a, cudaStream_t st);
 
+// Weight-prefetching tensor-core GEMV (gemv_pf.cu); SPECTRA_ERR_UNSUPPORTED
+// (nothing launched) when the arguments do not meet its layout conditions.
+int launch_gemv_pf(const GemvArgs& a, cudaStream_t st);
+
 struct DequantArgs {
   const uint8_t* packed; int64_t w_rs;
   const __half* scales; int64_t s_rs, s_cs;

@@ -1,5 +1,5 @@
-// Raw-code tensor-core GEMV building blocks (mma.sync m16n8k16), shared by the
-// register-fed and the TMA-fed M=1 GEMV kernels.
+// Building blocks shared by the M=1 GEMV kernels: the raw-code tensor-core
+// step (mma.sync m16n8k16), bulk copies, warp reductions, SM count.
 #pragma once
 
 #include <stdint.h>
@@ -45,6 +45,64 @@ __host__ __device__ __forceinline__ int pair_k(int kk, int high, int layout) {
   const int j = kk >> 2, t = kk & 3;
   const int byte = 4 * j + 2 * high + (t >> 1);
   return code_k(byte, t & 1, layout);
+}
+
+template <int R>
+__device__ __forceinline__ void warp_transpose_reduce(float (&v)[R], int lane) {
+  // Each stage halves the rows a lane holds: the lower half-warp keeps the
+  // first half of its rows, the upper half keeps the second half.
+  int off = 16;
+#pragma unroll
+  for (int half = R / 2; half >= 1; half /= 2) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[i + half];
+      const float keep = up ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+    off >>= 1;
+  }
+  for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+}
+
+template <int R>
+__device__ __forceinline__ int reduced_row(int lane) {
+  int row = 0, off = 16;
+#pragma unroll
+  for (int half = R / 2; half >= 1; half /= 2) {
+    if (lane & off) row += half;
+    off >>= 1;
+  }
+  return row;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+               : "memory");
+}
+
+// Same copy with an L2 cache-policy hint (from createpolicy).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+      "l"(src), "r"(bytes), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar))), "l"(policy)
+      : "memory");
+}
+
+inline int device_sms(int dev) {
+  static int sms[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (sms[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    sms[dev] = v;
+  }
+  return sms[dev];
 }
 
 }  // namespace spectra

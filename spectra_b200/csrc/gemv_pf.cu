@@ -1,0 +1,531 @@
+// M=1 W4A16 decode GEMV, weight-prefetching variant for sm_100a (replaces
+// spectra/kernels.py:16-184 for contiguous, 16-byte-aligned weights with K a
+// multiple of 512; other layouts take gemv.cu).
+//
+// Why a second kernel
+//   A decoder layer at M=1 is a chain of small GEMVs (0.5-10 MB of weights
+//   each), so per-launch latency (the previous kernel's completion, then the
+//   activation load, then the first weight loads) outweighs the streaming
+//   time.  This kernel moves every weight byte of a CTA into shared memory
+//   BEFORE it waits on the previous kernel (programmatic dependent launch):
+//   weights, scales, zero points and outlier weights are never written by the
+//   kernels of this library that release their dependents early, so reading
+//   them ahead of the dependency wait is safe.  Only the copies run early:
+//   compute there would take issue slots from the previous kernel.
+//
+// Residency
+//   A CTA that owns one row block uses at most ~110 KB of shared memory and
+//   <= 96 registers per thread, so two CTAs -- this launch's and the next
+//   one's -- fit on one SM: while one computes, the next one's bulk copies
+//   already stream its weights.  A CTA that owns several row blocks takes its
+//   SM alone (>= 116 KB): sharing the SM with the next launch's prefetch was
+//   measured slower on a decoder layer (the co-resident copies delay this
+//   kernel's post-wait loads); the next launch's CTAs start on SMs as they free.
+//
+// Work decomposition
+//   Grid = min(16-row blocks, SMs); CTA c owns 16-row blocks [b0, b1) (an even
+//   split).  With contiguous weights a row block's codes, scales and zero
+//   points are three contiguous ranges: a "stage" is one row block, fetched by
+//   three bulk copies (a copy costs ~70-100 cycles to issue plus ~1 cycle per
+//   60 bytes, so few large copies keep the issue time far below the streaming
+//   time), with an L2 evict-first hint.  Warp 8 fills a ring of `ns` stages
+//   (every stage of the CTA up front when they fit) and refills it as stages
+//   free; warps 0-7 compute.
+//
+// Math (same as gemv.cu's tensor-core kernel)
+//   A unit is 16 rows x 8 groups (256 k).  Lane (g, c) of a warp holds rows g
+//   and g+8, groups 2c and 2c+1 of the unit; codes become bf16/fp16 16+q by
+//   one shift + LOP3, x sits block-diagonally in the B operand, so the 16
+//   m16n8k16 MMAs give D[row][group] = sum_k (16+q_k) x_k.  Per group:
+//   sum_k (q_k - z) s x_k = s (D - (16 + z) X_g), X_g = sum of the group's x.
+//   Warp w takes units w, w+8, ... of every stage and keeps one fp32 partial
+//   per row; the 8 partials of a row are summed in warp order at the end
+//   (deterministic), then the outlier columns (kernels.py:102-120), the bias
+//   (:122-124) and one rounding to y's dtype.
+#include "common.cuh"
+#include "gemv.h"
+#include "gemv_mma.cuh"
+#include "sm100_ptx.cuh"
+
+namespace spectra {
+
+namespace {
+
+constexpr int kPfComputeWarps = 8;
+constexpr int kPfThreads = (kPfComputeWarps + 1) * 32;
+constexpr int kPfMaxStages = 8;
+constexpr size_t kPfSmemPair = 110 * 1024;    // two CTAs per SM (228 KB per SM)
+constexpr size_t kPfSmemSolo = 200 * 1024;    // one CTA per SM
+constexpr size_t kPfSoloFloor = 116 * 1024;   // more than half an SM's shared memory: one CTA per SM
+constexpr int kPfKQuantum = 512;
+constexpr int kXpWords = 20;  // staged x pairs per group: 16 + 4 pad (conflict-free B-fragment loads)
+
+struct PfParams {
+  GemvArgs a;
+  int ns;                          // ring stages
+  int off_sc, off_z, stage_bytes;  // offsets inside one stage (codes at 0)
+  int off_x, off_xsum, off_xos, off_red, off_ow, off_stage;
+  int rows_max;
+  int vec_x;                       // x contiguous and 16-byte aligned
+};
+
+__device__ int g_gemv_pf_timeouts;  // stuck pipeline waits since load (diagnostic)
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// 16-byte shared load when `pred`, zeros otherwise (no request for the
+// lanes that are off).
+__device__ __forceinline__ uint4 lds128_if(const uint4* p, bool pred) {
+  uint4 v;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %5, 0;\n\t"
+      "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
+      "@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n\t}"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(int(pred)));
+  return v;
+}
+
+__device__ __forceinline__ void compute_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kPfComputeWarps * 32) : "memory");
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kPfThreads, 2) gemv_pf_kernel(const __grid_constant__ PfParams kp) {
+  using namespace sm100;
+  const GemvArgs& p = kp.a;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full_bar[kPfMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kPfMaxStages];
+  __shared__ __align__(8) uint64_t ow_bar;
+  __shared__ int s_abort;
+  __shared__ int s_zero;
+
+  pdl_trigger();
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t nblk = (int64_t(p.N) + 15) / 16;
+  const int64_t b0 = (nblk * blockIdx.x) / gridDim.x;
+  const int64_t b1 = (nblk * (blockIdx.x + 1)) / gridDim.x;
+  const int nrb = int(b1 - b0);
+  const int64_t r_begin = b0 * 16;
+  const int64_t r_end = (int64_t(p.N) < b1 * 16) ? int64_t(p.N) : b1 * 16;
+  const int nrows = int(r_end - r_begin);
+  const int G = p.K / kGroup;
+
+  // Outlier weights of this CTA's rows: the 16-byte-aligned middle by one bulk
+  // copy, the ragged tail (< 16 B) by plain loads, both before the wait.
+  const int ow_es = p.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  const bool ow_staged = kp.off_ow >= 0 && p.n_out > 0;
+  const int64_t ow_b0 = r_begin * p.n_out * ow_es;
+  const int64_t ow_b1 = r_end * p.n_out * ow_es;
+  const int64_t ow_a0 = ow_b0 & ~int64_t(15);
+  const int64_t ow_a1 = ow_b1 & ~int64_t(15);
+
+  if (tid == 0) {
+    s_abort = 0;
+    s_zero = 0;
+    for (int s = 0; s < kp.ns; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kPfComputeWarps);
+    }
+    mbar_init(&ow_bar, 2);  // the bulk copy's arrival + the tail writer's
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kPfComputeWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint64_t policy;  // streamed once: first out of L2
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+      const int G = p.K / kGroup;
+      const uint32_t code_row = uint32_t(p.K / 2), sc_row = uint32_t(G * 2), z_row = uint32_t(G);
+      if (ow_staged) {
+        const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
+        mbar_arrive_expect_tx(&ow_bar, uint32_t(ow_a1 - ow_a0));
+        if (ow_a1 > ow_a0) bulk_g2s_hint(smem + kp.off_ow, ow_src + ow_a0, uint32_t(ow_a1 - ow_a0), &ow_bar, policy);
+        for (int64_t bt = ow_a1; bt < ow_b1; ++bt) smem[kp.off_ow + (bt - ow_a0)] = ow_src[bt];
+        mbar_arrive(&ow_bar);
+      }
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      for (int rb = 0; rb < nrb; ++rb) {
+        const int64_t row0 = r_begin + int64_t(rb) * 16;
+        const uint32_t rv = uint32_t(r_end - row0 < 16 ? r_end - row0 : 16);
+        if (issued >= kp.ns && !mbar_wait(&empty_bar[s], ph ^ 1u, &s_abort)) {
+          s_abort = 1;
+          atomicAdd(&g_gemv_pf_timeouts, 1);
+          break;
+        }
+        uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
+        mbar_arrive_expect_tx(&full_bar[s], rv * (code_row + sc_row + z_row));
+        bulk_g2s_hint(st, p.packed + row0 * code_row, rv * code_row, &full_bar[s], policy);
+        bulk_g2s_hint(st + kp.off_sc, reinterpret_cast<const uint8_t*>(p.scales) + row0 * sc_row, rv * sc_row,
+                      &full_bar[s], policy);
+        bulk_g2s_hint(st + kp.off_z, p.zeros + row0 * z_row, rv * z_row, &full_bar[s], policy);
+        ++issued;
+        if (++s == kp.ns) { s = 0; ph ^= 1u; }
+      }
+      // Leave no copy in flight: wait (bounded) for the last stages issued.
+      const int tail = issued < kp.ns ? issued : kp.ns;
+      for (int i = 0; i < tail; ++i) {
+        if (s == 0) { s = kp.ns; ph ^= 1u; }
+        --s;
+        (void)mbar_wait(&full_bar[s], ph, &s_zero);
+      }
+      if (ow_staged) (void)mbar_wait(&ow_bar, 0, &s_zero);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- compute
+  uint32_t* xp = reinterpret_cast<uint32_t*>(smem + kp.off_x);  // [G][kXpWords] x pairs, MMA order
+  float* xsum = reinterpret_cast<float*>(smem + kp.off_xsum);   // [G]
+  float* xos = reinterpret_cast<float*>(smem + kp.off_xos);     // [n_out]
+  float* red = reinterpret_cast<float*>(smem + kp.off_red);     // [rows_max][8]
+  constexpr int kCT = kPfComputeWarps * 32;
+
+  constexpr int kOutPerThread = 2;
+  int64_t oidx[kOutPerThread];
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m) {
+    const int j = tid + m * kCT;
+    oidx[m] = (j < p.n_out) ? load_index(p.idx, j, p.idx_dtype) : -1;
+  }
+
+  pdl_wait();  // x (and y) may belong to the previous kernel
+
+  // Stage x: 16 pairs per group in the MMA's k order (bit-exact copies of x)
+  // and the per-group sums X_g.  x is read through L2 only (ld.global.cg):
+  // it may have been written by the kernel this one waited for.
+  // x at the outlier features: loaded now, stored to shared memory only
+  // before the final pass, so their latency overlaps everything below.
+  uint32_t xo_raw[kOutPerThread];
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m)
+    xo_raw[m] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_bits_cg(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0u;
+  const bool marlin = p.layout == SPECTRA_LAYOUT_MARLIN;
+  if (kp.vec_x) {
+    // Thread t stages 8 consecutive features (one 16-byte load): quarter
+    // q = t & 3 of a group, 4 pairs.  Marlin pairs (k, k+2), even-odd (k, k+4).
+    const int q = tid & 3;
+    const int sbase = marlin ? 8 * (q & 1) + (q >> 1) : 4 * q;
+    const int sstep = marlin ? 2 : 1;
+    const int nchunk = p.K / 8;  // a multiple of 64: every warp's 32 chunks are all valid or all not
+    const uint4* xv = reinterpret_cast<const uint4*>(p.x);
+    constexpr int kB = 4;
+    for (int c0 = tid; c0 < nchunk; c0 += kB * kCT) {
+      uint4 raw[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int c = c0 + b * kCT;
+        raw[b] = c < nchunk ? __ldcg(xv + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int c = c0 + b * kCT;
+        if (c >= nchunk) break;  // warp-uniform: the shuffles below see the whole warp
+        const uint32_t w0 = raw[b].x, w1 = raw[b].y, w2 = raw[b].z, w3 = raw[b].w;
+        uint32_t pr[4];
+        if (marlin) {
+          pr[0] = prmt(w0, w1, 0x5410u); pr[1] = prmt(w0, w1, 0x7632u);
+          pr[2] = prmt(w2, w3, 0x5410u); pr[3] = prmt(w2, w3, 0x7632u);
+        } else {
+          pr[0] = prmt(w0, w2, 0x5410u); pr[1] = prmt(w0, w2, 0x7632u);
+          pr[2] = prmt(w1, w3, 0x5410u); pr[3] = prmt(w1, w3, 0x7632u);
+        }
+        float t = 0.f;
+        const uint32_t wv[4] = {w0, w1, w2, w3};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if constexpr (BF16) {
+            t += __uint_as_float(wv[i] << 16) + __uint_as_float(wv[i] & 0xFFFF0000u);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
+            t += f.x + f.y;
+          }
+        }
+        const int gl = c >> 2;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xp[gl * kXpWords + sbase + i * sstep] = pr[i];
+        t += __shfl_xor_sync(0xffffffffu, t, 1);
+        t += __shfl_xor_sync(0xffffffffu, t, 2);
+        if (q == 0) xsum[gl] = t;
+      }
+    }
+  } else {
+    // Strided x: one pair per lane, 16 lanes per group.
+    const int nstage = G * 16;
+    const unsigned short* xh = reinterpret_cast<const unsigned short*>(p.x);
+    for (int e = tid; e < nstage; e += kCT) {  // nstage = 16 G, a multiple of kCT: uniform trip count
+      const int gl = e >> 4, kk = e & 15;
+      const int64_t kb = int64_t(gl) * kGroup;
+      const uint32_t lo = __ldcg(xh + (kb + pair_k(kk, 0, p.layout)) * p.x_stride);
+      const uint32_t hi = __ldcg(xh + (kb + pair_k(kk, 1, p.layout)) * p.x_stride);
+      xp[gl * kXpWords + kk] = lo | (hi << 16);
+      float t = BF16 ? (__uint_as_float(lo << 16) + __uint_as_float(hi << 16))
+                     : (__half2float(__ushort_as_half(uint16_t(lo))) + __half2float(__ushort_as_half(uint16_t(hi))));
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if ((lane & 15) == 0) xsum[gl] = t;
+    }
+  }
+  compute_bar();
+
+  // ------------------------------------------------------------ main loop
+  uint32_t magic_reg;
+  asm volatile("mov.b32 %0, %1;" : "=r"(magic_reg) : "n"(BF16 ? 0x41804180u : 0x4C004C00u));  // 16.0 x2
+  const int g = lane >> 2, c = lane & 3;
+  // Block-diagonal B: only lanes (g = 2c) and (g = 2c + 1) hold x (columns 2c
+  // and 2c + 1 of the unit); the loads of the other lanes are predicated off.
+  const bool lane_a = (lane % 9) == 0;  // lanes 0, 9, 18, 27
+  const bool lane_b = (lane % 9) == 4;  // lanes 4, 13, 22, 31
+  uint32_t bA[16], bB[16];
+  int cached_kb = -1;
+  int s = 0;
+  uint32_t ph = 0;
+  const int KB = p.K >> 8;                     // 256-feature units per row
+  const int cs = p.K / 2, ss = G * 2, zs = G;  // stage row strides (bytes)
+  for (int rb = 0; rb < nrb; ++rb) {
+    float acc0 = 0.f, acc1 = 0.f;
+    bool ready = mbar_wait(&full_bar[s], ph, &s_abort);
+    ready = __all_sync(0xffffffffu, ready);
+    if (!ready) {
+      if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
+    } else {
+      const uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
+      for (int kb = warp; kb < KB; kb += kPfComputeWarps) {
+        const int gg = kb * 8 + 2 * c;  // this lane's first group
+        if (kb != cached_kb) {          // warp-uniform
+          cached_kb = kb;
+          const uint4* srcA = reinterpret_cast<const uint4*>(xp + gg * kXpWords);
+          const uint4* srcB = reinterpret_cast<const uint4*>(xp + (gg + 1) * kXpWords);
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const uint4 ta = lds128_if(srcA + qq, lane_a);
+            const uint4 tb = lds128_if(srcB + qq, lane_b);
+            bA[4 * qq] = ta.x; bA[4 * qq + 1] = ta.y; bA[4 * qq + 2] = ta.z; bA[4 * qq + 3] = ta.w;
+            bB[4 * qq] = tb.x; bB[4 * qq + 1] = tb.y; bB[4 * qq + 2] = tb.z; bB[4 * qq + 3] = tb.w;
+          }
+        }
+        const uint8_t* c0p = st + g * cs + gg * kGroupBytes;
+        const uint8_t* c1p = c0p + 8 * cs;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(c0p);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(c1p);
+        const uint4 w2 = *reinterpret_cast<const uint4*>(c0p + kGroupBytes);
+        const uint4 w3 = *reinterpret_cast<const uint4*>(c1p + kGroupBytes);
+        const uint8_t* sp = st + kp.off_sc + g * ss + gg * 2;
+        const uint32_t sc0 = *reinterpret_cast<const uint32_t*>(sp);
+        const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(sp + 8 * ss);
+        const uint8_t* zp = st + kp.off_z + g * zs + gg;
+        const uint32_t zr0 = *reinterpret_cast<const uint16_t*>(zp);
+        const uint32_t zr1 = *reinterpret_cast<const uint16_t*>(zp + 8 * zs);
+        const uint32_t wa[4][4] = {{w0.x, w0.y, w0.z, w0.w},
+                                   {w1.x, w1.y, w1.z, w1.w},
+                                   {w2.x, w2.y, w2.z, w2.w},
+                                   {w3.x, w3.y, w3.z, w3.w}};
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#define SPECTRA_PF_MMA(ACC, T)                                                                                  \
+  mma16816<BF16>(ACC, pair_code<BF16, T>(wa[0][j], magic_reg), pair_code<BF16, T>(wa[1][j], magic_reg),           \
+                 pair_code<BF16, T>(wa[2][j], magic_reg), pair_code<BF16, T>(wa[3][j], magic_reg),                \
+                 bA[4 * j + T], bB[4 * j + T]);
+          SPECTRA_PF_MMA(d, 0) SPECTRA_PF_MMA(e, 1) SPECTRA_PF_MMA(d, 2) SPECTRA_PF_MMA(e, 3)
+#undef SPECTRA_PF_MMA
+        }
+        // d + e = {D[g][gA], D[g][gA+1], D[g+8][gA], D[g+8][gA+1]}
+        const float XA = xsum[gg], XB = xsum[gg + 1];
+        const uint32_t scs[2] = {sc0, sc1};
+        const uint32_t zrs[2] = {zr0, zr1};
+        float rs[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float sa = __half2float(__ushort_as_half(uint16_t(scs[h] & 0xFFFFu)));
+          const float sb = __half2float(__ushort_as_half(uint16_t(scs[h] >> 16)));
+          const float za = __uint_as_float((zrs[h] & 0xFFu) | kMagic) - 8388608.0f + 16.0f;
+          const float zb = __uint_as_float(((zrs[h] >> 8) & 0xFFu) | kMagic) - 8388608.0f + 16.0f;
+          rs[h] = sa * fmaf(-za, XA, d[2 * h] + e[2 * h]) + sb * fmaf(-zb, XB, d[2 * h + 1] + e[2 * h + 1]);
+        }
+        acc0 += rs[0];
+        acc1 += rs[1];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    if (++s == kp.ns) { s = 0; ph ^= 1u; }
+    // rows g, g+8 of this row block: sum the 4 lanes of a quad
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    if (c == 0) {
+      red[(rb * 16 + g) * kPfComputeWarps + warp] = acc0;
+      red[(rb * 16 + g + 8) * kPfComputeWarps + warp] = acc1;
+    }
+  }
+
+  // --------------------------------------- outlier columns, bias, one store
+  // Eight threads per row: the outlier dot product split over them, then the
+  // 8 warp partials in warp order.
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m) {
+    const int j = tid + m * kCT;
+    if (j < p.n_out) xos[j] = bits_to_float(xo_raw[m], p.x_dtype);
+  }
+  for (int j = tid + kOutPerThread * kCT; j < p.n_out; j += kCT) {
+    const int64_t k = load_index(p.idx, j, p.idx_dtype);
+    xos[j] = (k >= 0 && k < p.K) ? load_as_float_cg(p.x, k * p.x_stride, p.x_dtype) : 0.f;
+  }
+  bool ow_ok = true;
+  if (ow_staged) {
+    ow_ok = mbar_wait(&ow_bar, 0, &s_abort);
+    ow_ok = __all_sync(0xffffffffu, ow_ok);
+    if (!ow_ok && lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
+  }
+  compute_bar();
+  constexpr int tpr = 8;
+  const int sub = tid & (tpr - 1);
+  const uint8_t* ow_smem = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);
+  for (int i0 = 0; i0 < nrows; i0 += kCT / tpr) {  // CTA-uniform trips
+    const int i = i0 + tid / tpr;
+    float v = 0.f;
+    if (i < nrows && p.n_out > 0 && ow_ok) {
+      if (ow_staged) {
+        const uint8_t* orow = ow_smem + int64_t(i) * p.n_out * ow_es;
+        if (ow_es == 4) {
+          for (int j = sub; j < p.n_out; j += tpr) v = fmaf(xos[j], reinterpret_cast<const float*>(orow)[j], v);
+        } else if (p.ow_dtype == SPECTRA_DT_BF16) {
+          for (int j = sub; j < p.n_out; j += tpr)
+            v = fmaf(xos[j], __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(orow)[j]) << 16), v);
+        } else {
+          for (int j = sub; j < p.n_out; j += tpr)
+            v = fmaf(xos[j], __half2float(reinterpret_cast<const __half*>(orow)[j]), v);
+        }
+      } else {
+        for (int j = sub; j < p.n_out; j += tpr)
+          v = fmaf(xos[j], load_as_float(p.ow, (r_begin + i) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype), v);
+      }
+    }
+#pragma unroll
+    for (int o = tpr >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (sub == 0 && i < nrows) {
+      const float4 r0 = *reinterpret_cast<const float4*>(red + i * kPfComputeWarps);
+      const float4 r1 = *reinterpret_cast<const float4*>(red + i * kPfComputeWarps + 4);
+      float y = r0.x;
+      y += r0.y; y += r0.z; y += r0.w;
+      y += r1.x; y += r1.y; y += r1.z; y += r1.w;
+      y += v;
+      const int64_t row = r_begin + i;
+      if (p.bias) y += load_as_float_cg(p.bias, row, p.bias_dtype);
+      store_from_float(p.y, row * p.y_stride, p.y_dtype, y);
+    }
+  }
+}
+
+inline size_t r16(size_t v) { return (v + 15) & ~size_t(15); }
+inline size_t r128(size_t v) { return (v + 127) & ~size_t(127); }
+inline bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
+
+template <bool BF16>
+int launch_pf(const PfParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
+  auto kern = gemv_pf_kernel<BF16>;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmemSolo));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, kp));
+}
+
+}  // namespace
+
+int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
+  if (!pf_path_enabled()) return SPECTRA_ERR_UNSUPPORTED;
+  if (a.x_dtype != SPECTRA_DT_BF16 && a.x_dtype != SPECTRA_DT_F16) return SPECTRA_ERR_UNSUPPORTED;
+  if (a.K % kPfKQuantum != 0) return SPECTRA_ERR_UNSUPPORTED;
+  const int G = a.K / kGroup;
+  // contiguous weights: a row block is one range per tensor
+  if (!al16(a.packed) || a.w_rs != a.K / 2) return SPECTRA_ERR_UNSUPPORTED;
+  if (a.s_cs != 1 || a.s_rs != G || !al16(a.scales)) return SPECTRA_ERR_UNSUPPORTED;
+  if (a.z_cs != 1 || a.z_rs != G || !al16(a.zeros)) return SPECTRA_ERR_UNSUPPORTED;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
+
+  PfParams kp{};
+  kp.a = a;
+  const int64_t nblk = (int64_t(a.N) + 15) / 16;
+  const int64_t grid = std::min<int64_t>(nblk, device_sms(dev));
+  const int64_t rb_max = (nblk + grid - 1) / grid;
+  kp.rows_max = int(rb_max * 16);
+  kp.vec_x = (a.x_stride == 1 && al16(a.x)) ? 1 : 0;
+  // CTAs that own several row blocks run alone on their SM: sharing it with
+  // the next launch's prefetching CTA slowed a decoder layer by ~12 % (the
+  // co-resident copies delay this kernel's post-wait loads); CTAs with one
+  // row block finish quickly and keep the two-per-SM footprint.
+  const bool solo = rb_max > 1;
+  const size_t budget = solo ? kPfSmemSolo : kPfSmemPair;
+
+  size_t off = 0;
+  kp.off_x = 0;
+  off = r16(size_t(G) * kXpWords * 4);
+  kp.off_xsum = int(off);
+  off = r16(off + size_t(G) * 4);
+  kp.off_xos = int(off);
+  off = r16(off + size_t(a.n_out) * 4);
+  kp.off_red = int(off);
+  off = r16(off + size_t(kp.rows_max) * kPfComputeWarps * 4);
+
+  const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  const bool ow_contig = a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && al16(a.ow);
+  for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
+    size_t o = off;
+    kp.off_ow = -1;
+    if (try_ow) {
+      kp.off_ow = int(o);
+      o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
+    }
+    kp.off_stage = int(r128(o));
+    if (size_t(kp.off_stage) >= budget) continue;
+    const size_t avail = budget - size_t(kp.off_stage);
+    kp.off_sc = 16 * (a.K / 2);
+    kp.off_z = kp.off_sc + 16 * G * 2;
+    const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(G));
+    kp.stage_bytes = int(sb);
+    const int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), rb_max});
+    if (ns < std::min<int64_t>(2, rb_max)) continue;  // no overlap of copies and compute: gemv.cu does better
+    kp.ns = int(ns);
+    size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * size_t(sb);
+    if (solo) smem = std::max(smem, kPfSoloFloor);
+    return a.x_dtype == SPECTRA_DT_BF16 ? launch_pf<true>(kp, grid, smem, dev, st)
+                                        : launch_pf<false>(kp, grid, smem, dev, st);
+  }
+  return SPECTRA_ERR_UNSUPPORTED;
+}
+
+}  // namespace spectra

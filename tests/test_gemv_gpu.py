@@ -289,3 +289,114 @@ def test_dequant_bit_exact(marlin, golden_dir):
     # the reference test's own dequant (tests/test_kernels.py:31-36)
     w32 = SK.dequantize(_t(d["packed"]), _t(d["scales"].view(np.float16)), _t(d["zeros"]), marlin_layout=True)
     np.testing.assert_array_equal(w32.cpu().numpy().view(np.uint32), d["w_deq_f32"].view(np.uint32))
+
+
+# ---------------------------------------------------------------------------
+# weight-prefetching kernel (K % 512 == 0, 16-byte aligned unit-stride weights)
+# ---------------------------------------------------------------------------
+
+def _padded_weights(fmt, N, K, pad_rows=3, pad_p=32, pad_s=8, pad_z=16):
+    """Weights as [:N, :width] views of wider, 16-byte-aligned slots."""
+    slot_p = torch.zeros(N + pad_rows, K // 2 + pad_p, dtype=torch.uint8)
+    slot_p[:N, :K // 2] = torch.from_numpy(fmt["packed"])
+    slot_s = torch.zeros(N + pad_rows, K // 32 + pad_s, dtype=torch.float16)
+    slot_s[:N, :K // 32] = torch.from_numpy(fmt["scales"])
+    slot_z = torch.zeros(N + pad_rows, K // 32 + pad_z, dtype=torch.uint8)
+    slot_z[:N, :K // 32] = torch.from_numpy(fmt["zeros"])
+    return (slot_p.to(DEV)[:N, :K // 2], slot_s.to(DEV)[:N, :K // 32], slot_z.to(DEV)[:N, :K // 32])
+
+
+@pytest.mark.parametrize("padded", [False, True])
+@pytest.mark.parametrize("xdt", ["bf16", "f16"])
+@pytest.mark.parametrize("marlin", [True, False])
+def test_gemv_prefetch_strided_x(padded, xdt, marlin):
+    """Strided x with contiguous weights (the prefetching kernel's scalar x
+    staging) and with weights bound as views of wider slots (the other kernel)."""
+    K, N = 3072, 1000
+    fmt = random_format(N, K, 31, seed=40, ow_dtype=xdt)
+    if padded:
+        p, s, z = _padded_weights(fmt, N, K)
+    else:
+        p, s, z = _t(fmt["packed"]), _t(fmt["scales"]), _t(fmt["zeros"])
+    xw = act(1, 2 * K, seed=41, dtype=xdt).to(DEV)
+    x = xw[:, 1::2]
+    idx = _t(fmt["outlier_idx"])
+    ow = fmt["outlier_w_t"].to(DEV)
+    y = SK.fused_w4a16_gemv_hdsq(x, p, s, z, outlier_idx=idx, outlier_w=ow, marlin_layout=marlin)
+    torch.cuda.synchronize()
+    y_exact, y_round, od = oracle_gemv(fmt, x.cpu(), marlin)
+    assert_close_to_oracle(out_f64(y).reshape(-1), y_exact, y_round, od, f"padded={padded} {xdt} marlin={marlin}")
+
+
+@pytest.mark.parametrize("N", [1, 16, 31, 148 * 16 * 2 + 5, 148 * 16 * 7 - 9])
+def test_gemv_prefetch_row_splits(N):
+    """One row, one block, a ragged block, CTAs with 2-3 and 7 row blocks
+    (the last refills the stage ring at K=4096)."""
+    K = 4096 if N > 5000 else 1024
+    fmt = random_format(N, K, 7, seed=N + 3)
+    x = act(1, K, seed=N + 4, dtype="bf16")
+    y = out_f64(run_gemv(fmt, x)).reshape(-1)
+    y_exact, y_round, od = oracle_gemv(fmt, x)
+    assert_close_to_oracle(y, y_exact, y_round, od, f"N={N}")
+
+
+def test_gemv_prefetch_f32_outliers_and_bias_f32_out():
+    K, N = 2048, 600
+    fmt = random_format(N, K, 40, seed=42, ow_dtype="f32")
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(43)).to(torch.bfloat16)
+    x = act(1, K, seed=44, dtype="bf16")
+    out = torch.empty(1, N, dtype=torch.float32, device=DEV)
+    y = run_gemv(fmt, x, bias=bias, out=out)
+    assert y.dtype == torch.float32
+    # the reference rounds to x's dtype (bf16) before storing into out
+    y_exact, y_round, od = oracle_gemv(fmt, x, bias=bias)
+    assert_close_to_oracle(out_f64(y).reshape(-1), y_exact, y_round, od, "f32 ow / out")
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_gemv_chained_launches_respect_stream_order(graph):
+    """Each GEMV reads the previous one's output and writes the buffer the one
+    before it read: the dependency wait must order both the read of x and the
+    write of y, eagerly and inside a CUDA graph."""
+    D, steps = 2048, 12
+    fmts = [random_format(D, D, 5, seed=50 + i) for i in range(3)]
+    ws = [(_t(f["packed"]), _t(f["scales"]), _t(f["zeros"]), _t(f["outlier_idx"]), f["outlier_w_t"].to(DEV))
+          for f in fmts]
+    x0 = act(1, D, seed=60, dtype="bf16").to(DEV) * 0.05
+    bufs = [torch.empty(1, D, dtype=torch.bfloat16, device=DEV) for _ in range(2)]
+
+    def chain():
+        bufs[0].copy_(x0)
+        for i in range(steps):
+            p, s, z, idx, ow = ws[i % 3]
+            SK.fused_w4a16_gemv_hdsq(bufs[i % 2], p, s, z, outlier_idx=idx, outlier_w=ow,
+                                     out=bufs[(i + 1) % 2], marlin_layout=True)
+            # keep magnitudes bounded without leaving the GEMV chain
+            SK.fused_w4a16_gemv_hdsq(bufs[(i + 1) % 2], p, s, z, outlier_idx=idx, outlier_w=ow,
+                                     out=bufs[i % 2], marlin_layout=True)
+
+    if graph:
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            chain()
+        torch.cuda.current_stream().wait_stream(st)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            chain()
+        g.replay()
+    else:
+        chain()
+    torch.cuda.synchronize()
+    got = bufs[0].clone()
+
+    # replay step by step with a full synchronisation between launches
+    ref = [torch.empty_like(b) for b in bufs]
+    ref[0].copy_(x0)
+    for i in range(steps):
+        p, s, z, idx, ow = ws[i % 3]
+        for src, dst in ((i % 2, (i + 1) % 2), ((i + 1) % 2, i % 2)):
+            SK.fused_w4a16_gemv_hdsq(ref[src], p, s, z, outlier_idx=idx, outlier_w=ow, out=ref[dst],
+                                     marlin_layout=True)
+            torch.cuda.synchronize()
+    assert torch.equal(got, ref[0])
