@@ -56,9 +56,10 @@ METRIC = "W4A16 GEMV GB/s at M=1 (Llama-3.2-1B decoder layer q/k/v/o/gate/up/dow
 WORKLOAD = "Llama-3.2-1B decoder layer, 7 linears at M=1, bf16 activations"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one gate_proj GEMV launch (K=2048, N=8192, 21
-# outlier columns), from one ncu capture of this kernel on this shape
-# (dram__bytes_read.sum + dram__bytes_write.sum): equal to the algorithmic bytes.
-GATE_TRAFFIC_BYTES = 10_350_848
+# outlier columns), from one ncu capture of the weight-prefetching kernel on
+# this shape (dram__bytes_read.sum + dram__bytes_write.sum): equal to the
+# algorithmic bytes.
+GATE_TRAFFIC_BYTES = 10_363_904
 
 
 def algorithmic_bytes(M: int, N: int, K: int, n_out: int, act_bytes: int = 2) -> int:
@@ -468,7 +469,7 @@ def run_gpu(args, world, rank, local):
             "gpu_launches": 7 * args.steps * 2,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": GATE_TRAFFIC_BYTES,
-                         "kernel": "GEMV gate_proj K=2048 N=8192 M=1", "peak_source": peak_kind,
+                         "kernel": "gemv_pf_kernel gate_proj K=2048 N=8192 M=1", "peak_source": peak_kind,
                          "avg_launch_us": round(dt_gate * 1e6, 3)},
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": cpu,
