@@ -21,6 +21,11 @@ GEMM ``batched_w4a16_gemm`` on the Llama-3-8B linear shapes (K x N) 4096x4096,
 4096x1024, 4096x14336, 14336x4096 at M = 16, 64, 256 (TFLOP/s), and the M = 1
 GEMV on the same shapes (GB/s), weights rotated over copies totalling > 3 x L2.
 
+It also carries ``sharded_sweep``: the Llama-3-70B linears
+(8192x8192, 8192x28672, 28672x8192, 8192x128256 lm_head; heavy-tailed weights) at
+M = 1 and 32, column-sharded over the job's GPUs with one NCCL all-gather, L2
+flushed before every call, slowest rank counted.
+
 ``--impl reference`` times the reference's CPU formula for the same layer
 (``oracle/cpu_path.py``) on the host cores instead.  Under torchrun (N>1) every
 rank runs the same single-GPU workload on its own layer copies (replicas:
@@ -276,6 +281,73 @@ def gemm_sweep(SK, dev) -> dict:
             "note": "TFLOP/s counts 2*M*N*(K + outlier columns); GB/s counts the algorithmic bytes"}
 
 
+SHARD_SHAPES = [(8192, 8192), (8192, 28672), (28672, 8192), (8192, 128256)]  # (K, N), Llama-3-70B
+SHARD_MS = (1, 32)
+
+
+def sharded_sweep(world: int, dev) -> dict:
+    """BASELINE config 5 at the job's world size: each Llama-3-70B linear
+    column-sharded over the ranks (``spectra_b200.sharded.ShardedW4A16Linear``:
+    this rank's rows with the production kernels, one NCCL all-gather), weights
+    heavy-tailed (Student-t, 3 degrees of freedom, scaled to std 0.02, the same
+    seed on every rank) and quantised on the device.  Each rank rotates over
+    copies of its shard totalling > 3 x L2; calls run back to back after one
+    barrier as CUDA-graph replays of one rotation (all-gathers included), CUDA
+    events around the whole run, slowest rank counted."""
+    import copy as _copy
+    from spectra_b200 import compress as C
+    from spectra_b200.sharded import ShardedW4A16Linear
+    res = []
+    for K, N in SHARD_SHAPES:
+        g = torch.Generator(device=dev).manual_seed(5000 + K + N)
+        z = torch.randn(4, N, K, generator=g, device=dev)
+        t = z[0] / torch.sqrt((z[1] ** 2 + z[2] ** 2 + z[3] ** 2) / 3.0)  # Student-t, df = 3
+        del z
+        w = (t * (0.02 / 3.0 ** 0.5)).to(torch.float16)  # var(t_3) = 3
+        del t
+        c = C.compress_linear(w)
+        del w
+        n_out = c.outlier_idx.numel()
+        lin = ShardedW4A16Linear(c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w, None,
+                                 marlin_layout=True, device=dev)
+        del c
+        shard_bytes = algorithmic_bytes(0, lin.rows, K, n_out)
+        lins = [lin]
+        while len(lins) < 16 and len(lins) * shard_bytes < 3 * 126e6:
+            cl = _copy.copy(lin)
+            cl.packed, cl.scales, cl.zeros = lin.packed.clone(), lin.scales.clone(), lin.zeros.clone()
+            cl.outlier_w = None if lin.outlier_w is None else lin.outlier_w.clone()
+            lins.append(cl)
+        torch.cuda.empty_cache()
+        for M in SHARD_MS:
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            for l_ in lins:
+                l_.forward(x)
+            # one rotation captured on every rank (the all-gathers included), so
+            # the host launch cost of the Python module is outside the timing
+            barrier(world)
+            gr = capture(lambda: [l_.forward(x) for l_ in lins], dev)
+            gr.replay()
+            reps = 5
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            dt = time_events(lambda: [gr.replay() for _ in range(reps)], dev) / (reps * len(lins))
+            dt = max_over_ranks(dt, world, dev)
+            torch.cuda.synchronize(dev)
+            del gr  # graphs holding NCCL calls go before the process group does
+            byts = algorithmic_bytes(M, N, K, n_out)
+            r = {"K": K, "N": N, "M": M, "n_out": n_out, "us": round(dt * 1e6, 2),
+                 "gbs": round(byts / dt / 1e9, 1)}
+            if M > 1:
+                r["tflops"] = round(2.0 * M * N * (K + n_out) / dt / 1e12, 2)
+            res.append(r)
+        del lin, lins
+        torch.cuda.empty_cache()
+    return {"gpus": world, "sharding": f"N-columns over {world} GPU(s), NCCL all-gather" if world > 1
+            else "1 GPU (no collective)", "l2": "each rank rotates over shard copies > 3 x L2",
+            "unit": "GB/s of the whole layer's algorithmic bytes; TFLOP/s for M > 1", "results": res}
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -486,6 +558,7 @@ def run_gpu(args, world, rank, local):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
+    shard = sharded_sweep(world, dev) if not args.no_sharded_sweep else None
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
 
@@ -516,6 +589,7 @@ def run_gpu(args, world, rank, local):
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": cpu,
             "gemm_sweep": sweep,
+            "sharded_sweep": shard,
         }
         print(json.dumps(line), flush=True)
     for g in singles + [cycle, g_gate]:
@@ -530,6 +604,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the config-3 GEMM/GEMV shape sweep")
+    ap.add_argument("--no-sharded-sweep", action="store_true",
+                    help="skip the config-5 column-sharded Llama-3-70B layer sweep")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
