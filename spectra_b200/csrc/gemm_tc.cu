@@ -828,9 +828,11 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.nk = int((K + kStep - 1) / kStep);
   p.ncs = int((K + kCodeK - 1) / kCodeK);
   p.n_os = int((n_out + kStep - 1) / kStep);
-  const int sms = 148;
+  const int sms = 148;  // B200; one CTA per SM (~200 KB of shared memory)
   const int64_t ctas = int64_t(p.tiles_n) * p.m_chunks;
-  p.S = int(std::min<int64_t>(std::max<int64_t>(1, (sms + ctas / 2) / ctas), p.ncs));
+  // split K so that all CTAs fit in ONE wave: rounding up (e.g. 32 tiles x 5 =
+  // 160 CTAs) leaves a second wave of a few CTAs that doubles the time
+  p.S = int(std::min<int64_t>(std::max<int64_t>(1, sms / ctas), p.ncs));
   p.act_stage_bytes = p.MT * 128;
   p.code_stages = p.MT <= 32 ? 6 : p.MT <= 64 ? 5 : p.MT <= 128 ? 4 : 3;
   const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 3 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot +
