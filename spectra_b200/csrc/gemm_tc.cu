@@ -447,21 +447,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t a_unit = tmem + a_col0 + uint32_t(asl.idx * 128);
-        for (int j = 0; j < ns && live; ++j, ar.next()) {
-          if (!mbar_wait(afull + ar.idx, ar.phase, &s_abort)) {
-            s_abort = 1;
-            atomicAdd(&g_gemm_timeouts, 1);
-            live = false;
-            break;
+        if (AS > kStepsPerCode) {
+          // The act ring holds more than a unit: wait for all its steps, issue
+          // the unit's MMAs back to back, then free the slots (one wait-MMA-
+          // commit round per step cost ~600 cycles a step at small MT).
+          int slot[kStepsPerCode];
+          for (int j = 0; j < ns; ++j, ar.next()) {
+            slot[j] = ar.idx;
+            if (!mbar_wait(afull + ar.idx, ar.phase, &s_abort)) {
+              s_abort = 1;
+              atomicAdd(&g_gemm_timeouts, 1);
+              live = false;
+              break;
+            }
           }
+          if (!live) break;
           tc_fence_after();
-          const uint32_t b_base = smem_u32(act_st + ar.idx * act_bytes);
-          for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
-            const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
-            mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
-                   (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+          for (int j = 0; j < ns; ++j) {
+            const uint32_t b_base = smem_u32(act_st + slot[j] * act_bytes);
+            for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
+              const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
+              mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
+                     (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+            }
           }
-          mma_commit(afree + ar.idx);
+          for (int j = 0; j < ns; ++j) mma_commit(afree + slot[j]);
+        } else {
+          // fewer act slots than steps in a unit: release each slot after its
+          // own step, or the producer could never fill the unit's last step
+          for (int j = 0; j < ns && live; ++j, ar.next()) {
+            if (!mbar_wait(afull + ar.idx, ar.phase, &s_abort)) {
+              s_abort = 1;
+              atomicAdd(&g_gemm_timeouts, 1);
+              live = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b_base = smem_u32(act_st + ar.idx * act_bytes);
+            for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
+              const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
+              mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
+                     (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+            }
+            mma_commit(afree + ar.idx);
+          }
         }
         if (!live) break;
         mma_commit(mdone + u % kDone);
