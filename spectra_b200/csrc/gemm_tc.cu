@@ -43,6 +43,7 @@
 #include "common.cuh"
 #include "gemm.h"
 #include "sm100_ptx.cuh"
+#include "tmap.h"
 
 // Split-K scratch of spectra_w4a16_gemm_noalloc, laid out like a caller
 // workspace (tile counters, then fp32 partials).  Zero when the module loads;
@@ -833,7 +834,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+}  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     cudaDriverEntryPointQueryResult q;
@@ -844,8 +847,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   }
   return fn;
 }
-
-}  // namespace
 
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   GemmPlan p{};
@@ -912,7 +913,7 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   const GemmPlan pl = plan_gemm(a.M, a.N, a.K, a.n_out);
   if (pl.tmem_cols > 512 || pl.smem > kMaxDynSmem || pl.act_stages < 3) return SPECTRA_ERR_UNSUPPORTED;
   if (pl.S > 1 && (ws == nullptr || ws_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
-  auto enc = encode_fn();
+  auto enc = tensor_map_encoder();
   if (!enc) return SPECTRA_ERR_UNSUPPORTED;
   const bool bf16 = a.a_dtype == SPECTRA_DT_BF16;
   const int G = a.K / kGroup;

@@ -46,6 +46,7 @@
 #include "gemv.h"
 #include "gemv_mma.cuh"
 #include "sm100_ptx.cuh"
+#include "tmap.h"
 
 namespace spectra {
 
@@ -57,16 +58,28 @@ constexpr size_t kPfSmemPair = 110 * 1024;    // two CTAs per SM (228 KB per SM)
 constexpr size_t kPfSmemSolo = 200 * 1024;    // one CTA per SM
 constexpr size_t kPfSoloFloor = 116 * 1024;   // more than half an SM's shared memory: one CTA per SM
 constexpr int kPfKQuantum = 512;
+constexpr int kPfMaxWholeK = 4096;  // largest K whose row block is one stage (38 KB)
+constexpr int kPfChunk = 2048;      // features per tensor-map stage (codes box: 256 words)
 constexpr int kXpWords = 20;  // staged x pairs per group: 16 + 4 pad (conflict-free B-fragment loads)
 
 struct PfParams {
   GemvArgs a;
   int ns;                          // ring stages
+  int kc, nkc;                     // input features per stage (a multiple of 512), stages per row block
   int off_sc, off_z, stage_bytes;  // offsets inside one stage (codes at 0)
   int off_x, off_xsum, off_xos, off_red, off_ow, off_stage;
   int rows_max;
   int vec_x;                       // x contiguous and 16-byte aligned
 };
+
+// Tensor maps of the chunked mode; the contiguous mode passes an empty struct
+// (no 384 bytes of unused kernel parameters per launch).
+template <bool CHUNKED>
+struct PfMaps {
+  CUtensorMap c, s, z;  // codes, scales, zero points
+};
+template <>
+struct PfMaps<false> {};
 
 __device__ int g_gemv_pf_timeouts;  // stuck pipeline waits since load (diagnostic)
 
@@ -98,9 +111,9 @@ __device__ __forceinline__ void compute_bar() {
 // NG compute groups of 8 warps plus one copy warp.  NG = 1: <= 96 registers,
 // so two CTAs fit on an SM; NG = 2 (CTAs with many row blocks): group i takes
 // row blocks i, i+2, ...
-template <bool BF16, int NG>
+template <bool BF16, int NG, bool CHUNKED>
 __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1)
-    gemv_pf_kernel(const __grid_constant__ PfParams kp) {
+    gemv_pf_kernel(const __grid_constant__ PfMaps<CHUNKED> maps, const __grid_constant__ PfParams kp) {
   constexpr int kPfComputeWarps = NG * kPfGroupWarps;
   using namespace sm100;
   const GemvArgs& p = kp.a;
@@ -163,22 +176,35 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       int s = 0;
       uint32_t ph = 0;
       int issued = 0;
-      for (int rb = 0; rb < nrb; ++rb) {
+      bool ok = true;
+      const uint32_t tma_tx = 16u * uint32_t(kp.kc / 2 + kp.kc / 16 + kp.kc / 32);  // full boxes (OOB rows: zeros)
+      const int nkc = CHUNKED ? kp.nkc : 1;
+      for (int rb = 0; rb < nrb && ok; ++rb) {
         const int64_t row0 = r_begin + int64_t(rb) * 16;
         const uint32_t rv = uint32_t(r_end - row0 < 16 ? r_end - row0 : 16);
-        if (issued >= kp.ns && !mbar_wait(&empty_bar[s], ph ^ 1u, &s_abort)) {
-          s_abort = 1;
-          atomicAdd(&g_gemv_pf_timeouts, 1);
-          break;
+        for (int ch = 0; ch < nkc; ++ch) {
+          if (issued >= kp.ns && !mbar_wait(&empty_bar[s], ph ^ 1u, &s_abort)) {
+            s_abort = 1;
+            atomicAdd(&g_gemv_pf_timeouts, 1);
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
+          if constexpr (CHUNKED) {
+            mbar_arrive_expect_tx(&full_bar[s], tma_tx);
+            tma_load_2d_hint(st, &maps.c, ch * (kp.kc / 8), int(row0), &full_bar[s], policy);
+            tma_load_2d_hint(st + kp.off_sc, &maps.s, ch * (kp.kc / 32), int(row0), &full_bar[s], policy);
+            tma_load_2d_hint(st + kp.off_z, &maps.z, ch * (kp.kc / 32), int(row0), &full_bar[s], policy);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[s], rv * (code_row + sc_row + z_row));
+            bulk_g2s_hint(st, p.packed + row0 * code_row, rv * code_row, &full_bar[s], policy);
+            bulk_g2s_hint(st + kp.off_sc, reinterpret_cast<const uint8_t*>(p.scales) + row0 * sc_row, rv * sc_row,
+                          &full_bar[s], policy);
+            bulk_g2s_hint(st + kp.off_z, p.zeros + row0 * z_row, rv * z_row, &full_bar[s], policy);
+          }
+          ++issued;
+          if (++s == kp.ns) { s = 0; ph ^= 1u; }
         }
-        uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[s], rv * (code_row + sc_row + z_row));
-        bulk_g2s_hint(st, p.packed + row0 * code_row, rv * code_row, &full_bar[s], policy);
-        bulk_g2s_hint(st + kp.off_sc, reinterpret_cast<const uint8_t*>(p.scales) + row0 * sc_row, rv * sc_row,
-                      &full_bar[s], policy);
-        bulk_g2s_hint(st + kp.off_z, p.zeros + row0 * z_row, rv * z_row, &full_bar[s], policy);
-        ++issued;
-        if (++s == kp.ns) { s = 0; ph ^= 1u; }
       }
       // Leave no copy in flight: wait (bounded) for the last stages issued.
       const int tail = issued < kp.ns ? issued : kp.ns;
@@ -296,22 +322,30 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   const bool lane_b = (lane % 9) == 4;  // lanes 4, 13, 22, 31
   uint32_t bA[16], bB[16];
   int cached_kb = -1;
-  const int KB = p.K >> 8;                     // 256-feature units per row
-  const int cs = p.K / 2, ss = G * 2, zs = G;  // stage row strides (bytes)
+  const int KB = p.K >> 8;                               // 256-feature units per row
+  const int kc = CHUNKED ? kp.kc : p.K;                 // features per stage
+  const int KBc = kc >> 8;                               // 256-feature units per stage
+  const int cs = kc / 2, ss = kc / 16, zs = kc / 32;     // stage row strides (bytes)
+  const int nkc = CHUNKED ? kp.nkc : 1;
   const int grp = NG == 1 ? 0 : warp / kPfGroupWarps;  // compute group, and warp inside it
   const int w8 = NG == 1 ? warp : warp % kPfGroupWarps;
-  int s = grp;  // ring slot of row block rb (ns >= 2 whenever NG == 2)
+  int s = grp;  // ring slot of the stage (NG == 2 only with one stage per row block, ns >= 2)
   uint32_t ph = 0;
   for (int rb = grp; rb < nrb; rb += NG) {
     float acc0 = 0.f, acc1 = 0.f;
+    for (int ch = 0; ch < nkc; ++ch) {
     bool ready = mbar_wait(&full_bar[s], ph, &s_abort);
     ready = __all_sync(0xffffffffu, ready);
     if (!ready) {
       if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
     } else {
       const uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
-      for (int kb = w8; kb < KB; kb += kPfGroupWarps) {
-        const int gg = kb * 8 + 2 * c;  // this lane's first group
+      const int kb0 = ch * KBc;                         // first unit of this stage along K
+      const int kbn = KB - kb0 < KBc ? KB - kb0 : KBc;  // units in this stage
+      for (int kl = w8; kl < kbn; kl += kPfGroupWarps) {
+        const int kb = kb0 + kl;
+        const int gl = kl * 8 + 2 * c;  // this lane's first group inside the stage
+        const int gg = kb * 8 + 2 * c;  // ... inside the row
         if (kb != cached_kb) {          // warp-uniform
           cached_kb = kb;
           const uint4* srcA = reinterpret_cast<const uint4*>(xp + gg * kXpWords);
@@ -324,16 +358,16 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
             bB[4 * qq] = tb.x; bB[4 * qq + 1] = tb.y; bB[4 * qq + 2] = tb.z; bB[4 * qq + 3] = tb.w;
           }
         }
-        const uint8_t* c0p = st + g * cs + gg * kGroupBytes;
+        const uint8_t* c0p = st + g * cs + gl * kGroupBytes;
         const uint8_t* c1p = c0p + 8 * cs;
         const uint4 w0 = *reinterpret_cast<const uint4*>(c0p);
         const uint4 w1 = *reinterpret_cast<const uint4*>(c1p);
         const uint4 w2 = *reinterpret_cast<const uint4*>(c0p + kGroupBytes);
         const uint4 w3 = *reinterpret_cast<const uint4*>(c1p + kGroupBytes);
-        const uint8_t* sp = st + kp.off_sc + g * ss + gg * 2;
+        const uint8_t* sp = st + kp.off_sc + g * ss + gl * 2;
         const uint32_t sc0 = *reinterpret_cast<const uint32_t*>(sp);
         const uint32_t sc1 = *reinterpret_cast<const uint32_t*>(sp + 8 * ss);
-        const uint8_t* zp = st + kp.off_z + g * zs + gg;
+        const uint8_t* zp = st + kp.off_z + g * zs + gl;
         const uint32_t zr0 = *reinterpret_cast<const uint16_t*>(zp);
         const uint32_t zr1 = *reinterpret_cast<const uint16_t*>(zp + 8 * zs);
         const uint32_t wa[4][4] = {{w0.x, w0.y, w0.z, w0.w},
@@ -370,6 +404,9 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);
+    s += NG;
+    if (s >= kp.ns) { s -= kp.ns; ph ^= 1u; }
+    }  // stages of the row block
     // rows g, g+8 of this row block: sum the 4 lanes of a quad
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -379,8 +416,6 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       red[(rb * 16 + g) * kPfGroupWarps + w8] = acc0;
       red[(rb * 16 + g + 8) * kPfGroupWarps + w8] = acc1;
     }
-    s += NG;
-    if (s >= kp.ns) { s -= kp.ns; ph ^= 1u; }
   }
 
   // --------------------------------------- outlier columns, bias, one store
@@ -445,9 +480,9 @@ inline size_t r16(size_t v) { return (v + 15) & ~size_t(15); }
 inline size_t r128(size_t v) { return (v + 127) & ~size_t(127); }
 inline bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
-template <bool BF16, int NG>
-int launch_pf(const PfParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
-  auto kern = gemv_pf_kernel<BF16, NG>;
+template <bool BF16, int NG, bool CHUNKED>
+int launch_pf(const PfMaps<true>& all_maps, const PfParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
+  auto kern = gemv_pf_kernel<BF16, NG, CHUNKED>;
   static bool attr_set[kMaxDevices] = {};
   if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmemSolo));
@@ -466,7 +501,32 @@ int launch_pf(const PfParams& kp, int64_t grid, size_t smem, int dev, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, kp));
+  PfMaps<CHUNKED> maps;
+  if constexpr (CHUNKED) maps = all_maps;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, maps, kp));
+}
+
+// Tensor maps of the three weight tensors for [16 rows x kc features] boxes:
+// codes as 32-bit words, scales as 16-bit, zero points as bytes.
+bool encode_stage_maps(const GemvArgs& a, int kc, PfMaps<true>& maps) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int G = a.K / kGroup;
+  cuuint32_t es[2] = {1, 1};
+  cuuint64_t dc[2] = {cuuint64_t(a.K / 8), cuuint64_t(a.N)}, sc[1] = {cuuint64_t(a.w_rs)};
+  cuuint32_t bc[2] = {cuuint32_t(kc / 8), 16};
+  cuuint64_t dg[2] = {cuuint64_t(G), cuuint64_t(a.N)};
+  cuuint64_t ss[1] = {cuuint64_t(a.s_rs) * 2}, zs[1] = {cuuint64_t(a.z_rs)};
+  cuuint32_t bg[2] = {cuuint32_t(kc / kGroup), 16};
+  return enc(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(a.packed), dc, sc, bc, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+         enc(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<__half*>(a.scales), dg, ss, bg, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+         enc(&maps.z, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.zeros), dg, zs, bg, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
@@ -476,10 +536,13 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
   if (a.x_dtype != SPECTRA_DT_BF16 && a.x_dtype != SPECTRA_DT_F16) return SPECTRA_ERR_UNSUPPORTED;
   if (a.K % kPfKQuantum != 0) return SPECTRA_ERR_UNSUPPORTED;
   const int G = a.K / kGroup;
-  // contiguous weights: a row block is one range per tensor
-  if (!al16(a.packed) || a.w_rs != a.K / 2) return SPECTRA_ERR_UNSUPPORTED;
-  if (a.s_cs != 1 || a.s_rs != G || !al16(a.scales)) return SPECTRA_ERR_UNSUPPORTED;
-  if (a.z_cs != 1 || a.z_rs != G || !al16(a.zeros)) return SPECTRA_ERR_UNSUPPORTED;
+  if (!al16(a.packed) || !al16(a.scales) || !al16(a.zeros) || a.s_cs != 1 || a.z_cs != 1)
+    return SPECTRA_ERR_UNSUPPORTED;
+  // Contiguous weights: a stage is a whole row block, three contiguous bulk
+  // copies, when two such stages fit.  Otherwise stages of [16 rows x 2048
+  // features] by tensor maps (row pitches must be multiples of 16 bytes).
+  const bool contiguous = a.w_rs == a.K / 2 && a.s_rs == G && a.z_rs == G;
+  const bool pitches16 = a.w_rs % 16 == 0 && (a.s_rs * 2) % 16 == 0 && a.z_rs % 16 == 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -487,6 +550,8 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
 
   PfParams kp{};
   kp.a = a;
+  PfMaps<true> maps;
+  memset(&maps, 0, sizeof(maps));
   const int64_t nblk = (int64_t(a.N) + 15) / 16;
   const int64_t grid = std::min<int64_t>(nblk, device_sms(dev));
   const int64_t rb_max = (nblk + grid - 1) / grid;
@@ -511,6 +576,11 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
 
   const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   const bool ow_contig = a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && al16(a.ow);
+  for (int chunked = contiguous ? 0 : 1; chunked <= 1; ++chunked) {
+  if (chunked && !pitches16) break;
+  kp.kc = chunked ? std::min(a.K, kPfChunk) : a.K;
+  kp.nkc = (a.K + kp.kc - 1) / kp.kc;
+  if (chunked && !encode_stage_maps(a, kp.kc, maps)) break;
   for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
     size_t o = off;
     kp.off_ow = -1;
@@ -521,23 +591,30 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
     kp.off_stage = int(r128(o));
     if (size_t(kp.off_stage) >= budget) continue;
     const size_t avail = budget - size_t(kp.off_stage);
-    kp.off_sc = 16 * (a.K / 2);
-    kp.off_z = kp.off_sc + 16 * G * 2;
-    const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(G));
+    kp.off_sc = 16 * (kp.kc / 2);                    // codes [16][kc/2 B]
+    kp.off_z = kp.off_sc + 16 * (kp.kc / 16);        // scales [16][kc/16 B]
+    const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(kp.kc / kGroup));  // zero points [16][kc/32 B]
     kp.stage_bytes = int(sb);
-    const int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), rb_max});
-    if (ns < std::min<int64_t>(2, rb_max)) continue;  // no overlap of copies and compute: gemv.cu does better
+    const int64_t units = rb_max * kp.nkc;
+    const int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), units});
+    if (ns < std::min<int64_t>(2, units)) continue;  // no overlap of copies and compute: gemv.cu does better
     kp.ns = int(ns);
     size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * size_t(sb);
     if (solo) smem = std::max(smem, kPfSoloFloor);
-    // Two compute groups (16 warps) for CTAs with >= 5 row blocks: measured 10 % faster on
-    // 4096 x 14336; with fewer row blocks one group keeps room on the SM for the next
-    // launch's prefetching CTA (two groups were slower on a 1B decoder layer).
+    // Two compute groups (16 warps) for CTAs with >= 5 row blocks of one
+    // stage each: measured 10 % faster on 4096 x 14336; with fewer row blocks
+    // one group keeps room on the SM for the next launch's prefetching CTA
+    // (two groups were slower on a 1B decoder layer).
+    const bool bf = a.x_dtype == SPECTRA_DT_BF16;
+    if (chunked)
+      return bf ? launch_pf<true, 1, true>(maps, kp, grid, smem, dev, st)
+                : launch_pf<false, 1, true>(maps, kp, grid, smem, dev, st);
     if (rb_max >= 5)
-      return a.x_dtype == SPECTRA_DT_BF16 ? launch_pf<true, 2>(kp, grid, smem, dev, st)
-                                          : launch_pf<false, 2>(kp, grid, smem, dev, st);
-    return a.x_dtype == SPECTRA_DT_BF16 ? launch_pf<true, 1>(kp, grid, smem, dev, st)
-                                        : launch_pf<false, 1>(kp, grid, smem, dev, st);
+      return bf ? launch_pf<true, 2, false>(maps, kp, grid, smem, dev, st)
+                : launch_pf<false, 2, false>(maps, kp, grid, smem, dev, st);
+    return bf ? launch_pf<true, 1, false>(maps, kp, grid, smem, dev, st)
+              : launch_pf<false, 1, false>(maps, kp, grid, smem, dev, st);
+  }
   }
   return SPECTRA_ERR_UNSUPPORTED;
 }
