@@ -28,9 +28,13 @@
 //   points are three contiguous ranges: a "stage" is one row block, fetched by
 //   three bulk copies (a copy costs ~70-100 cycles to issue plus ~1 cycle per
 //   60 bytes, so few large copies keep the issue time far below the streaming
-//   time), with an L2 evict-first hint.  Warp 8 fills a ring of `ns` stages
-//   (every stage of the CTA up front when they fit) and refills it as stages
-//   free; warps 0-7 compute.
+//   time), with an L2 evict-first hint.  When two such stages do not fit
+//   (K = 14336, 28672) or the rows are padded views, a stage is [16 rows x 2048
+//   features] instead, fetched by three 2D tensor-map copies (codes as 32-bit
+//   words, scales, zero points; rows past N read as zeros).  The last warp
+//   fills a ring of `ns` stages (every stage of the CTA up front when they fit)
+//   and refills it as stages free; the other warps compute: one group of 8,
+//   or two groups on alternate row blocks for CTAs with >= 5 row blocks.
 //
 // Math (same as gemv.cu's tensor-core kernel)
 //   A unit is 16 rows x 8 groups (256 k).  Lane (g, c) of a warp holds rows g
@@ -58,8 +62,7 @@ constexpr size_t kPfSmemPair = 110 * 1024;    // two CTAs per SM (228 KB per SM)
 constexpr size_t kPfSmemSolo = 200 * 1024;    // one CTA per SM
 constexpr size_t kPfSoloFloor = 116 * 1024;   // more than half an SM's shared memory: one CTA per SM
 constexpr int kPfKQuantum = 512;
-constexpr int kPfMaxWholeK = 4096;  // largest K whose row block is one stage (38 KB)
-constexpr int kPfChunk = 2048;      // features per tensor-map stage (codes box: 256 words)
+constexpr int kPfChunk = 2048;      // features per tensor-map stage (codes box: 256 32-bit words)
 constexpr int kXpWords = 20;  // staged x pairs per group: 16 + 4 pad (conflict-free B-fragment loads)
 
 struct PfParams {
