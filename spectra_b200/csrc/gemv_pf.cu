@@ -34,7 +34,8 @@
 //   words, scales, zero points; rows past N read as zeros).  The last warp
 //   fills a ring of `ns` stages (every stage of the CTA up front when they fit)
 //   and refills it as stages free; the other warps compute: one group of 8,
-//   or two groups on alternate row blocks for CTAs with >= 5 row blocks.
+//   or two groups on alternate stages (whole-row-block stages: CTAs with >= 5
+//   row blocks; chunked stages: every CTA that owns its SM).
 //
 // Math (same as gemv.cu's tensor-core kernel)
 //   A unit is 16 rows x 8 groups (256 k).  Lane (g, c) of a warp holds rows g
@@ -42,10 +43,10 @@
 //   one shift + LOP3, x sits block-diagonally in the B operand, so the 16
 //   m16n8k16 MMAs give D[row][group] = sum_k (16+q_k) x_k.  Per group:
 //   sum_k (q_k - z) s x_k = s (D - (16 + z) X_g), X_g = sum of the group's x.
-//   Warp w takes units w, w+8, ... of every stage and keeps one fp32 partial
-//   per row; the 8 partials of a row are summed in warp order at the end
-//   (deterministic), then the outlier columns (kernels.py:102-120), the bias
-//   (:122-124) and one rounding to y's dtype.
+//   Warp w of a group takes units w, w+8, ... of the group's stages and keeps
+//   one fp32 partial per row; the 8 (16) partials of a row are summed in warp
+//   order at the end (deterministic), then the outlier columns
+//   (kernels.py:102-120), the bias (:122-124) and one rounding to y's dtype.
 #include "common.cuh"
 #include "gemv.h"
 #include "gemv_mma.cuh"
@@ -63,6 +64,7 @@ constexpr size_t kPfSmemSolo = 200 * 1024;    // one CTA per SM
 constexpr size_t kPfSoloFloor = 116 * 1024;   // more than half an SM's shared memory: one CTA per SM
 constexpr int kPfKQuantum = 512;
 constexpr int kPfChunk = 2048;      // features per tensor-map stage (codes box: 256 32-bit words)
+constexpr int kPfMinWholeStages = 3;  // ring depth below which whole-row-block stages give way to chunks
 constexpr int kXpWords = 20;  // staged x pairs per group: 16 + 4 pad (conflict-free B-fragment loads)
 
 struct PfParams {
@@ -92,18 +94,17 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
-// 16-byte shared load when `pred`, zeros otherwise (no request for the
-// lanes that are off).
-__device__ __forceinline__ uint4 lds128_if(const uint4* p, bool pred) {
-  uint4 v;
+// 16-byte shared load into v when `pred`; v keeps its value otherwise (no
+// request for the lanes that are off).  The B fragments of the lanes that
+// never load stay at their initial zeros.
+__device__ __forceinline__ void lds128_keep(uint32_t& v0, uint32_t& v1, uint32_t& v2, uint32_t& v3, const uint4* p,
+                                            bool pred) {
   asm volatile(
       "{\n\t.reg .pred q;\n\t"
       "setp.ne.b32 q, %5, 0;\n\t"
-      "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
       "@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n\t}"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "+r"(v0), "+r"(v1), "+r"(v2), "+r"(v3)
       : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(int(pred)));
-  return v;
 }
 
 template <int NT>
@@ -112,8 +113,8 @@ __device__ __forceinline__ void compute_bar() {
 }
 
 // NG compute groups of 8 warps plus one copy warp.  NG = 1: <= 96 registers,
-// so two CTAs fit on an SM; NG = 2 (CTAs with many row blocks): group i takes
-// row blocks i, i+2, ...
+// so two CTAs fit on an SM; NG = 2 (CTAs that own their SM): group i takes
+// stages i, i+2, ... of the ring.
 template <bool BF16, int NG, bool CHUNKED>
 __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1)
     gemv_pf_kernel(const __grid_constant__ PfMaps<CHUNKED> maps, const __grid_constant__ PfParams kp) {
@@ -241,12 +242,6 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   // Stage x: 16 pairs per group in the MMA's k order (bit-exact copies of x)
   // and the per-group sums X_g.  x is read through L2 only (ld.global.cg):
   // it may have been written by the kernel this one waited for.
-  // x at the outlier features: loaded now, stored to shared memory only
-  // before the final pass, so their latency overlaps everything below.
-  uint32_t xo_raw[kOutPerThread];
-#pragma unroll
-  for (int m = 0; m < kOutPerThread; ++m)
-    xo_raw[m] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_bits_cg(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0u;
   const bool marlin = p.layout == SPECTRA_LAYOUT_MARLIN;
   if (kp.vec_x) {
     // Thread t stages 8 consecutive features (one 16-byte load): quarter
@@ -313,6 +308,15 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       if ((lane & 15) == 0) xsum[gl] = t;
     }
   }
+  // x at the outlier features, gathered after the x staging: the addresses
+  // come from index loads issued before the wait, which may still be in
+  // flight when the wait returns, and a gather ahead of the staging held its
+  // loads back (1.5 % on 2048 x 8192).  Stored to shared memory before the
+  // final pass.
+  uint32_t xo_raw[kOutPerThread];
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m)
+    xo_raw[m] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_bits_cg(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0u;
   compute_bar<kCT>();
 
   // ------------------------------------------------------------ main loop
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   // and 2c + 1 of the unit); the loads of the other lanes are predicated off.
   const bool lane_a = (lane % 9) == 0;  // lanes 0, 9, 18, 27
   const bool lane_b = (lane % 9) == 4;  // lanes 4, 13, 22, 31
-  uint32_t bA[16], bB[16];
+  uint32_t bA[16] = {}, bB[16] = {};
   int cached_kb = -1;
   const int KB = p.K >> 8;                               // 256-feature units per row
   const int kc = CHUNKED ? kp.kc : p.K;                 // features per stage
@@ -332,11 +336,21 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   const int nkc = CHUNKED ? kp.nkc : 1;
   const int grp = NG == 1 ? 0 : warp / kPfGroupWarps;  // compute group, and warp inside it
   const int w8 = NG == 1 ? warp : warp % kPfGroupWarps;
-  int s = grp;  // ring slot of the stage (NG == 2 only with one stage per row block, ns >= 2)
+  constexpr int RW = kPfComputeWarps;  // partials per row: one per compute warp
+  // Stages are consumed in issue order: stage si (row block si / nkc, chunk
+  // si % nkc) by group si % NG.  ns is even when NG == 2, so a group's previous
+  // use of a ring slot (stage si - ns) was its own and was waited for: the
+  // parity wait cannot complete on an older phase of the slot.
+  int s = 0;  // ring slot of stage si
   uint32_t ph = 0;
-  for (int rb = grp; rb < nrb; rb += NG) {
+  int si = 0;
+  for (int rb = 0; rb < nrb; ++rb) {
     float acc0 = 0.f, acc1 = 0.f;
-    for (int ch = 0; ch < nkc; ++ch) {
+    for (int ch = 0; ch < nkc; ++ch, ++si) {
+    if (NG > 1 && si % NG != grp) {
+      if (++s == kp.ns) { s = 0; ph ^= 1u; }
+      continue;
+    }
     bool ready = mbar_wait(&full_bar[s], ph, &s_abort);
     ready = __all_sync(0xffffffffu, ready);
     if (!ready) {
@@ -355,10 +369,8 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
           const uint4* srcB = reinterpret_cast<const uint4*>(xp + (gg + 1) * kXpWords);
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) {
-            const uint4 ta = lds128_if(srcA + qq, lane_a);
-            const uint4 tb = lds128_if(srcB + qq, lane_b);
-            bA[4 * qq] = ta.x; bA[4 * qq + 1] = ta.y; bA[4 * qq + 2] = ta.z; bA[4 * qq + 3] = ta.w;
-            bB[4 * qq] = tb.x; bB[4 * qq + 1] = tb.y; bB[4 * qq + 2] = tb.z; bB[4 * qq + 3] = tb.w;
+            lds128_keep(bA[4 * qq], bA[4 * qq + 1], bA[4 * qq + 2], bA[4 * qq + 3], srcA + qq, lane_a);
+            lds128_keep(bB[4 * qq], bB[4 * qq + 1], bB[4 * qq + 2], bB[4 * qq + 3], srcB + qq, lane_b);
           }
         }
         const uint8_t* c0p = st + g * cs + gl * kGroupBytes;
@@ -407,8 +419,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);
-    s += NG;
-    if (s >= kp.ns) { s -= kp.ns; ph ^= 1u; }
+    if (++s == kp.ns) { s = 0; ph ^= 1u; }
     }  // stages of the row block
     // rows g, g+8 of this row block: sum the 4 lanes of a quad
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
@@ -416,8 +427,8 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
     if (c == 0) {
-      red[(rb * 16 + g) * kPfGroupWarps + w8] = acc0;
-      red[(rb * 16 + g + 8) * kPfGroupWarps + w8] = acc1;
+      red[(rb * 16 + g) * RW + warp] = acc0;  // zero for a row block of the other group
+      red[(rb * 16 + g + 8) * RW + warp] = acc1;
     }
   }
 
@@ -466,11 +477,11 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
 #pragma unroll
     for (int o = tpr >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (sub == 0 && i < nrows) {
-      const float4 r0 = *reinterpret_cast<const float4*>(red + i * kPfGroupWarps);
-      const float4 r1 = *reinterpret_cast<const float4*>(red + i * kPfGroupWarps + 4);
-      float y = r0.x;
-      y += r0.y; y += r0.z; y += r0.w;
-      y += r1.x; y += r1.y; y += r1.z; y += r1.w;
+      const float4* rr = reinterpret_cast<const float4*>(red + i * RW);
+      float y = rr[0].x;
+      y += rr[0].y; y += rr[0].z; y += rr[0].w;
+#pragma unroll
+      for (int q = 1; q < RW / 4; ++q) { y += rr[q].x; y += rr[q].y; y += rr[q].z; y += rr[q].w; }
       y += v;
       const int64_t row = r_begin + i;
       if (p.bias) y += load_as_float_cg(p.bias, row, p.bias_dtype);
@@ -575,49 +586,71 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
   kp.off_xos = int(off);
   off = r16(off + size_t(a.n_out) * 4);
   kp.off_red = int(off);
-  off = r16(off + size_t(kp.rows_max) * kPfGroupWarps * 4);
 
   const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   const bool ow_contig = a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && al16(a.ow);
-  for (int chunked = contiguous ? 0 : 1; chunked <= 1; ++chunked) {
-  if (chunked && !pitches16) break;
-  kp.kc = chunked ? std::min(a.K, kPfChunk) : a.K;
-  kp.nkc = (a.K + kp.kc - 1) / kp.kc;
-  if (chunked && !encode_stage_maps(a, kp.kc, maps)) break;
-  for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
-    size_t o = off;
-    kp.off_ow = -1;
-    if (try_ow) {
-      kp.off_ow = int(o);
-      o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
-    }
-    kp.off_stage = int(r128(o));
-    if (size_t(kp.off_stage) >= budget) continue;
-    const size_t avail = budget - size_t(kp.off_stage);
+  const bool bf = a.x_dtype == SPECTRA_DT_BF16;
+  // Whole-row-block stages unless a CTA owns >= 5 row blocks and the ring
+  // holds fewer than kPfMinWholeStages of them: then the chunked mode's small
+  // stages keep more copies in flight and feed two compute groups (8192 x
+  // 28672: 48.8 -> 40.6 us; with 4 row blocks, 8192 x 8192, whole stages
+  // stayed 3 % faster).
+  bool prefer_chunked = false;
+  if (contiguous && pitches16 && rb_max >= 5) {
+    const size_t sb_whole = r128(16 * (size_t(a.K) / 2 + size_t(a.K) / 16 + size_t(a.K) / 32));
+    const size_t base = r16(off + size_t(kp.rows_max) * kPfGroupWarps * 4);
+    const int64_t ns_whole = base < budget ? int64_t((budget - base) / sb_whole) : 0;
+    prefer_chunked = ns_whole < std::min<int64_t>(rb_max, kPfMinWholeStages);
+  }
+  for (int chunked = (contiguous && !prefer_chunked) ? 0 : 1; chunked <= 1; ++chunked) {
+    if (chunked && !pitches16) break;
+    kp.kc = chunked ? std::min(a.K, kPfChunk) : a.K;
+    kp.nkc = (a.K + kp.kc - 1) / kp.kc;
+    if (chunked && !encode_stage_maps(a, kp.kc, maps)) break;
     kp.off_sc = 16 * (kp.kc / 2);                    // codes [16][kc/2 B]
     kp.off_z = kp.off_sc + 16 * (kp.kc / 16);        // scales [16][kc/16 B]
     const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(kp.kc / kGroup));  // zero points [16][kc/32 B]
     kp.stage_bytes = int(sb);
     const int64_t units = rb_max * kp.nkc;
-    const int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), units});
-    if (ns < std::min<int64_t>(2, units)) continue;  // no overlap of copies and compute: gemv.cu does better
-    kp.ns = int(ns);
-    size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * size_t(sb);
-    if (solo) smem = std::max(smem, kPfSoloFloor);
-    // Two compute groups (16 warps) for CTAs with >= 5 row blocks of one
-    // stage each: measured 10 % faster on 4096 x 14336; with fewer row blocks
-    // one group keeps room on the SM for the next launch's prefetching CTA
-    // (two groups were slower on a 1B decoder layer).
-    const bool bf = a.x_dtype == SPECTRA_DT_BF16;
-    if (chunked)
-      return bf ? launch_pf<true, 1, true>(maps, kp, grid, smem, dev, st)
-                : launch_pf<false, 1, true>(maps, kp, grid, smem, dev, st);
-    if (rb_max >= 5)
-      return bf ? launch_pf<true, 2, false>(maps, kp, grid, smem, dev, st)
-                : launch_pf<false, 2, false>(maps, kp, grid, smem, dev, st);
-    return bf ? launch_pf<true, 1, false>(maps, kp, grid, smem, dev, st)
-              : launch_pf<false, 1, false>(maps, kp, grid, smem, dev, st);
-  }
+    // Two compute groups (16 warps) on alternate stages when the CTA owns its
+    // SM: a stage's consumption (one 256-feature unit per warp) is latency
+    // bound at two warps per scheduler, and a ring of 19-39 KB stages is
+    // drained only as fast as it is consumed.  Contiguous stages (a whole row
+    // block each) keep one group below 5 row blocks: two were slower on a 1B
+    // decoder layer, where the CTA's SM is soon wanted by the next launch.
+    const int ng_pref = chunked ? (solo ? 2 : 1) : (rb_max >= 5 ? 2 : 1);
+    for (int ng = ng_pref; ng >= 1; --ng) {
+      const size_t off_ow = r16(off + size_t(kp.rows_max) * kPfGroupWarps * ng * 4);  // red: [rows][8 ng]
+      for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
+        size_t o = off_ow;
+        kp.off_ow = -1;
+        if (try_ow) {
+          kp.off_ow = int(o);
+          o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
+        }
+        kp.off_stage = int(r128(o));
+        if (size_t(kp.off_stage) >= budget) continue;
+        const size_t avail = budget - size_t(kp.off_stage);
+        int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), units});
+        if (ng == 2) ns &= ~int64_t(1);  // a ring slot's consecutive stages belong to one group
+        if (ns < std::min<int64_t>(2, units)) continue;  // no overlap of copies and compute: gemv.cu does better
+        kp.ns = int(ns);
+        size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * sb;
+        if (solo) smem = std::max(smem, kPfSoloFloor);
+        if (chunked) {
+          if (ng == 2)
+            return bf ? launch_pf<true, 2, true>(maps, kp, grid, smem, dev, st)
+                      : launch_pf<false, 2, true>(maps, kp, grid, smem, dev, st);
+          return bf ? launch_pf<true, 1, true>(maps, kp, grid, smem, dev, st)
+                    : launch_pf<false, 1, true>(maps, kp, grid, smem, dev, st);
+        }
+        if (ng == 2)
+          return bf ? launch_pf<true, 2, false>(maps, kp, grid, smem, dev, st)
+                    : launch_pf<false, 2, false>(maps, kp, grid, smem, dev, st);
+        return bf ? launch_pf<true, 1, false>(maps, kp, grid, smem, dev, st)
+                  : launch_pf<false, 1, false>(maps, kp, grid, smem, dev, st);
+      }
+    }
   }
   return SPECTRA_ERR_UNSUPPORTED;
 }

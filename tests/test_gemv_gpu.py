@@ -340,6 +340,19 @@ def test_gemv_prefetch_row_splits(N):
     assert_close_to_oracle(y, y_exact, y_round, od, f"N={N}")
 
 
+@pytest.mark.parametrize("K,N", [(8192, 148 * 16 * 5 + 7), (10240, 148 * 16 * 2 + 1), (5120, 148 * 16 * 5 + 3)])
+def test_gemv_prefetch_two_groups(K, N):
+    """Two compute groups on alternate stages: chunked stages for CTAs with
+    >= 5 row blocks of a large K (ragged last block), an odd number of chunks
+    per row block, and whole-row-block stages whose ring depth (3) is rounded
+    down to an even number."""
+    fmt = random_format(N, K, 9, seed=K + N)
+    x = act(1, K, seed=K + N + 1, dtype="bf16")
+    y = out_f64(run_gemv(fmt, x)).reshape(-1)
+    y_exact, y_round, od = oracle_gemv(fmt, x)
+    assert_close_to_oracle(y, y_exact, y_round, od, f"{K}x{N}")
+
+
 def test_gemv_prefetch_f32_outliers_and_bias_f32_out():
     K, N = 2048, 600
     fmt = random_format(N, K, 40, seed=42, ow_dtype="f32")
