@@ -75,6 +75,7 @@ struct PfParams {
   int off_x, off_xsum, off_xos, off_red, off_ow, off_stage;
   int rows_max;
   int vec_x;                       // x contiguous and 16-byte aligned
+  int ow_ring_rows;                // > 0: outlier rows stream through the freed ring, this many per piece
 };
 
 // Tensor maps of the chunked mode; the contiguous mode passes an empty struct
@@ -105,6 +106,24 @@ __device__ __forceinline__ void lds128_keep(uint32_t& v0, uint32_t& v1, uint32_t
       "@q ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n\t}"
       : "+r"(v0), "+r"(v1), "+r"(v2), "+r"(v3)
       : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(int(pred)));
+}
+
+// The bounded wait of sm100_ptx.cuh, inlined: at a call site with many live
+// registers the out-of-line slow path costs a stack frame and spills.
+__device__ __forceinline__ bool mbar_wait_inl(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  using namespace sm100;
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (i == 0 ? mbar_test(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 31) {
+      if (*abort) return false;
+      const uint64_t now = global_ns();
+      if (i == 31)
+        t0 = now;
+      else if (now - t0 > kWaitLimitNs)
+        return false;
+    }
+  }
 }
 
 template <int NT>
@@ -158,7 +177,9 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kPfGroupWarps);  // a stage is consumed by one group
     }
-    mbar_init(&ow_bar, 2);  // the bulk copy's arrival + the tail writer's
+    // Staged outlier weights: the bulk copy's arrival + the tail writer's;
+    // streamed through the ring: one arrival per piece.
+    mbar_init(&ow_bar, ow_staged ? 2 : 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -453,13 +474,46 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   compute_bar<kCT>();
   constexpr int tpr = 8;
   const int sub = tid & (tpr - 1);
-  const uint8_t* ow_smem = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);
-  for (int i0 = 0; i0 < nrows; i0 += kCT / tpr) {  // CTA-uniform trips
+  // Outlier weights too large to stage beside the ring stream through the
+  // ring itself once every stage is consumed (all its copies have landed:
+  // each was waited for), `ow_ring_rows` rows per piece by one bulk copy of
+  // the 16-byte-aligned middle plus plain loads of the ragged end.
+  const bool ow_ring = NG == 2 && kp.ow_ring_rows > 0 && p.n_out > 0;  // two groups only (host side too)
+  const bool ow_smem_rows = ow_staged || ow_ring;
+  const int piece_rows = ow_ring ? kp.ow_ring_rows : (nrows > 0 ? nrows : 1);
+  const int64_t row_bytes = int64_t(p.n_out) * ow_es;
+  const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
+  uint32_t ow_phase = 0;
+  for (int pr0 = 0; pr0 < nrows; pr0 += piece_rows) {  // CTA-uniform
+  const int pr1 = nrows - pr0 < piece_rows ? nrows : pr0 + piece_rows;
+  const uint8_t* ow_smem = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);  // row ow_row0
+  int ow_row0 = 0;
+  if (NG == 2 && ow_ring) {
+    const int64_t pb0 = (r_begin + pr0) * row_bytes, pb1 = (r_begin + pr1) * row_bytes;
+    const int64_t pa0 = pb0 & ~int64_t(15);
+    const int64_t pa1 = (pb1 & ~int64_t(15)) > pa0 ? (pb1 & ~int64_t(15)) : pa0;
+    uint8_t* ring = smem + kp.off_stage;
+    if (tid == 0) {
+      fence_proxy_async_smem();  // the ring's last reads were generic loads
+      mbar_arrive_expect_tx(&ow_bar, uint32_t(pa1 - pa0));
+      if (pa1 > pa0) bulk_g2s(ring, ow_src + pa0, uint32_t(pa1 - pa0), &ow_bar);
+    }
+    for (int64_t bt = pa1 + tid; bt < pb1; bt += kCT) ring[bt - pa0] = ow_src[bt];  // < 16 bytes
+    bool ok = mbar_wait_inl(&ow_bar, ow_phase, &s_abort);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
+    ow_ok = ow_ok && ok;
+    ow_phase ^= 1u;
+    compute_bar<kCT>();  // the plain tail stores
+    ow_smem = ring + (pb0 - pa0);
+    ow_row0 = pr0;
+  }
+  for (int i0 = pr0; i0 < pr1; i0 += kCT / tpr) {  // CTA-uniform trips
     const int i = i0 + tid / tpr;
     float v = 0.f;
-    if (i < nrows && p.n_out > 0 && ow_ok) {
-      if (ow_staged) {
-        const uint8_t* orow = ow_smem + int64_t(i) * p.n_out * ow_es;
+    if (i < pr1 && p.n_out > 0 && ow_ok) {
+      if (ow_smem_rows) {
+        const uint8_t* orow = ow_smem + int64_t(i - ow_row0) * row_bytes;
         if (ow_es == 4) {
           for (int j = sub; j < p.n_out; j += tpr) v = fmaf(xos[j], reinterpret_cast<const float*>(orow)[j], v);
         } else if (p.ow_dtype == SPECTRA_DT_BF16) {
@@ -476,7 +530,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
     }
 #pragma unroll
     for (int o = tpr >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (sub == 0 && i < nrows) {
+    if (sub == 0 && i < pr1) {
       const float4* rr = reinterpret_cast<const float4*>(red + i * RW);
       float y = rr[0].x;
       y += rr[0].y; y += rr[0].z; y += rr[0].w;
@@ -488,6 +542,8 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       store_from_float(p.y, row * p.y_stride, p.y_dtype, y);
     }
   }
+  if (ow_ring && pr1 < nrows) compute_bar<kCT>();  // the next piece overwrites the ring
+  }  // pieces
 }
 
 inline size_t r16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -635,6 +691,12 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
         if (ng == 2) ns &= ~int64_t(1);  // a ring slot's consecutive stages belong to one group
         if (ns < std::min<int64_t>(2, units)) continue;  // no overlap of copies and compute: gemv.cu does better
         kp.ns = int(ns);
+        kp.ow_ring_rows = 0;
+        if (!try_ow && ow_contig && ng == 2) {  // stream the outlier rows through the ring at the end
+          const int64_t row_bytes = int64_t(a.n_out) * ow_es, rpp = 32 * ng;
+          const int64_t rows = (ns * int64_t(sb) - 16) / row_bytes;
+          if (rows >= rpp) kp.ow_ring_rows = int(std::min<int64_t>(kp.rows_max, rows - rows % rpp));
+        }
         size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * sb;
         if (solo) smem = std::max(smem, kPfSoloFloor);
         if (chunked) {

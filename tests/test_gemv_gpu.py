@@ -353,6 +353,19 @@ def test_gemv_prefetch_two_groups(K, N):
     assert_close_to_oracle(y, y_exact, y_round, od, f"{K}x{N}")
 
 
+@pytest.mark.parametrize("n_out,ow_dt", [(601, "f32"), (700, "bf16")])
+def test_gemv_prefetch_outliers_streamed_through_ring(n_out, ow_dt):
+    """Outlier weights too large to stage beside the ring (144 rows per CTA)
+    stream through the freed ring after the main loop: 64 rows per piece,
+    2-3 pieces, the last CTA's rows ending off a 16-byte boundary."""
+    K, N = 2048, 148 * 16 * 8 + 5
+    fmt = random_format(N, K, n_out, seed=n_out, ow_dtype=ow_dt)
+    x = act(1, K, seed=n_out + 1, dtype="bf16")
+    y = out_f64(run_gemv(fmt, x)).reshape(-1)
+    y_exact, y_round, od = oracle_gemv(fmt, x)
+    assert_close_to_oracle(y, y_exact, y_round, od, f"n_out={n_out} {ow_dt}")
+
+
 def test_gemv_prefetch_f32_outliers_and_bias_f32_out():
     K, N = 2048, 600
     fmt = random_format(N, K, 40, seed=42, ow_dtype="f32")
