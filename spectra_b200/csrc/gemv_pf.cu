@@ -65,6 +65,7 @@ constexpr size_t kPfSoloFloor = 116 * 1024;   // more than half an SM's shared m
 constexpr int kPfKQuantum = 512;
 constexpr int kPfChunk = 2048;      // features per tensor-map stage (codes box: 256 32-bit words)
 constexpr int kPfMinWholeStages = 3;  // ring depth below which whole-row-block stages give way to chunks
+constexpr int kPfMinStagedRing = 4;   // ring depth below which staged outlier rows give way to streaming
 constexpr int kXpWords = 20;  // staged x pairs per group: 16 + 4 pad (conflict-free B-fragment loads)
 
 struct PfParams {
@@ -677,6 +678,18 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
     const int ng_pref = chunked ? (solo ? 2 : 1) : (rb_max >= 5 ? 2 : 1);
     for (int ng = ng_pref; ng >= 1; --ng) {
       const size_t off_ow = r16(off + size_t(kp.rows_max) * kPfGroupWarps * ng * 4);  // red: [rows][8 ng]
+      // Ring depth with the outlier rows staged beside the ring (o = its end)
+      // or not (they then stream through the ring after the main loop, two
+      // groups only): staging gives way when it leaves fewer than
+      // kPfMinStagedRing stages and streaming would leave more.
+      auto ring_depth = [&](size_t o) -> int64_t {
+        const size_t st_off = r128(o);
+        if (st_off >= budget) return 0;
+        int64_t n = std::min<int64_t>({int64_t(kPfMaxStages), int64_t((budget - st_off) / sb), units});
+        if (ng == 2) n &= ~int64_t(1);  // a ring slot's consecutive stages belong to one group
+        return n;
+      };
+      const int64_t ns_unstaged = ring_depth(off_ow);
       for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
         size_t o = off_ow;
         kp.off_ow = -1;
@@ -685,11 +698,9 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
           o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
         }
         kp.off_stage = int(r128(o));
-        if (size_t(kp.off_stage) >= budget) continue;
-        const size_t avail = budget - size_t(kp.off_stage);
-        int64_t ns = std::min<int64_t>({int64_t(kPfMaxStages), int64_t(avail / sb), units});
-        if (ng == 2) ns &= ~int64_t(1);  // a ring slot's consecutive stages belong to one group
+        const int64_t ns = ring_depth(o);
         if (ns < std::min<int64_t>(2, units)) continue;  // no overlap of copies and compute: gemv.cu does better
+        if (try_ow && ng == 2 && ns < std::min<int64_t>(kPfMinStagedRing, ns_unstaged)) continue;
         kp.ns = int(ns);
         kp.ow_ring_rows = 0;
         if (!try_ow && ow_contig && ng == 2) {  // stream the outlier rows through the ring at the end
