@@ -264,6 +264,13 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   // Stage x: 16 pairs per group in the MMA's k order (bit-exact copies of x)
   // and the per-group sums X_g.  x is read through L2 only (ld.global.cg):
   // it may have been written by the kernel this one waited for.
+  // x at the outlier features: loaded now, stored to shared memory only
+  // before the final pass, so their latency overlaps everything below (a
+  // gather after the x staging measured 1.5 % slower on a 1B decoder layer).
+  uint32_t xo_raw[kOutPerThread];
+#pragma unroll
+  for (int m = 0; m < kOutPerThread; ++m)
+    xo_raw[m] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_bits_cg(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0u;
   const bool marlin = p.layout == SPECTRA_LAYOUT_MARLIN;
   if (kp.vec_x) {
     // Thread t stages 8 consecutive features (one 16-byte load): quarter
@@ -330,15 +337,6 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       if ((lane & 15) == 0) xsum[gl] = t;
     }
   }
-  // x at the outlier features, gathered after the x staging: the addresses
-  // come from index loads issued before the wait, which may still be in
-  // flight when the wait returns, and a gather ahead of the staging held its
-  // loads back (1.5 % on 2048 x 8192).  Stored to shared memory before the
-  // final pass.
-  uint32_t xo_raw[kOutPerThread];
-#pragma unroll
-  for (int m = 0; m < kOutPerThread; ++m)
-    xo_raw[m] = (oidx[m] >= 0 && oidx[m] < p.K) ? load_bits_cg(p.x, oidx[m] * p.x_stride, p.x_dtype) : 0u;
   compute_bar<kCT>();
 
   // ------------------------------------------------------------ main loop
@@ -479,72 +477,78 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   // ring itself once every stage is consumed (all its copies have landed:
   // each was waited for), `ow_ring_rows` rows per piece by one bulk copy of
   // the 16-byte-aligned middle plus plain loads of the ragged end.
-  const bool ow_ring = NG == 2 && kp.ow_ring_rows > 0 && p.n_out > 0;  // two groups only (host side too)
-  const bool ow_smem_rows = ow_staged || ow_ring;
-  const int piece_rows = ow_ring ? kp.ow_ring_rows : (nrows > 0 ? nrows : 1);
   const int64_t row_bytes = int64_t(p.n_out) * ow_es;
-  const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
-  uint32_t ow_phase = 0;
-  for (int pr0 = 0; pr0 < nrows; pr0 += piece_rows) {  // CTA-uniform
-  const int pr1 = nrows - pr0 < piece_rows ? nrows : pr0 + piece_rows;
-  const uint8_t* ow_smem = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);  // row ow_row0
-  int ow_row0 = 0;
-  if (NG == 2 && ow_ring) {
-    const int64_t pb0 = (r_begin + pr0) * row_bytes, pb1 = (r_begin + pr1) * row_bytes;
-    const int64_t pa0 = pb0 & ~int64_t(15);
-    const int64_t pa1 = (pb1 & ~int64_t(15)) > pa0 ? (pb1 & ~int64_t(15)) : pa0;
-    uint8_t* ring = smem + kp.off_stage;
-    if (tid == 0) {
-      fence_proxy_async_smem();  // the ring's last reads were generic loads
-      mbar_arrive_expect_tx(&ow_bar, uint32_t(pa1 - pa0));
-      if (pa1 > pa0) bulk_g2s(ring, ow_src + pa0, uint32_t(pa1 - pa0), &ow_bar);
-    }
-    for (int64_t bt = pa1 + tid; bt < pb1; bt += kCT) ring[bt - pa0] = ow_src[bt];  // < 16 bytes
-    bool ok = mbar_wait_inl(&ow_bar, ow_phase, &s_abort);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok && lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
-    ow_ok = ow_ok && ok;
-    ow_phase ^= 1u;
-    compute_bar<kCT>();  // the plain tail stores
-    ow_smem = ring + (pb0 - pa0);
-    ow_row0 = pr0;
-  }
-  for (int i0 = pr0; i0 < pr1; i0 += kCT / tpr) {  // CTA-uniform trips
-    const int i = i0 + tid / tpr;
-    float v = 0.f;
-    if (i < pr1 && p.n_out > 0 && ow_ok) {
-      if (ow_smem_rows) {
-        const uint8_t* orow = ow_smem + int64_t(i - ow_row0) * row_bytes;
-        if (ow_es == 4) {
-          for (int j = sub; j < p.n_out; j += tpr) v = fmaf(xos[j], reinterpret_cast<const float*>(orow)[j], v);
-        } else if (p.ow_dtype == SPECTRA_DT_BF16) {
-          for (int j = sub; j < p.n_out; j += tpr)
-            v = fmaf(xos[j], __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(orow)[j]) << 16), v);
+  // Rows [pr0, pr1) of the CTA: outlier dot products (staged rows: row i at
+  // ow_rows + (i - ow_row0) * row_bytes), the partials in order, bias, store.
+  auto final_rows = [&](int pr0, int pr1, bool ow_in_smem, const uint8_t* ow_rows, int ow_row0, bool ow_ok) {
+    for (int i0 = pr0; i0 < pr1; i0 += kCT / tpr) {  // CTA-uniform trips
+      const int i = i0 + tid / tpr;
+      float v = 0.f;
+      if (i < pr1 && p.n_out > 0 && ow_ok) {
+        if (ow_in_smem) {
+          const uint8_t* orow = ow_rows + int64_t(i - ow_row0) * row_bytes;
+          if (ow_es == 4) {
+            for (int j = sub; j < p.n_out; j += tpr) v = fmaf(xos[j], reinterpret_cast<const float*>(orow)[j], v);
+          } else if (p.ow_dtype == SPECTRA_DT_BF16) {
+            for (int j = sub; j < p.n_out; j += tpr)
+              v = fmaf(xos[j], __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(orow)[j]) << 16), v);
+          } else {
+            for (int j = sub; j < p.n_out; j += tpr)
+              v = fmaf(xos[j], __half2float(reinterpret_cast<const __half*>(orow)[j]), v);
+          }
         } else {
           for (int j = sub; j < p.n_out; j += tpr)
-            v = fmaf(xos[j], __half2float(reinterpret_cast<const __half*>(orow)[j]), v);
+            v = fmaf(xos[j], load_as_float(p.ow, (r_begin + i) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype), v);
         }
-      } else {
-        for (int j = sub; j < p.n_out; j += tpr)
-          v = fmaf(xos[j], load_as_float(p.ow, (r_begin + i) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype), v);
+      }
+#pragma unroll
+      for (int o = tpr >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (sub == 0 && i < pr1) {
+        const float4* rr = reinterpret_cast<const float4*>(red + i * RW);
+        float y = rr[0].x;
+        y += rr[0].y; y += rr[0].z; y += rr[0].w;
+#pragma unroll
+        for (int q = 1; q < RW / 4; ++q) { y += rr[q].x; y += rr[q].y; y += rr[q].z; y += rr[q].w; }
+        y += v;
+        const int64_t row = r_begin + i;
+        if (p.bias) y += load_as_float_cg(p.bias, row, p.bias_dtype);
+        store_from_float(p.y, row * p.y_stride, p.y_dtype, y);
       }
     }
-#pragma unroll
-    for (int o = tpr >> 1; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (sub == 0 && i < pr1) {
-      const float4* rr = reinterpret_cast<const float4*>(red + i * RW);
-      float y = rr[0].x;
-      y += rr[0].y; y += rr[0].z; y += rr[0].w;
-#pragma unroll
-      for (int q = 1; q < RW / 4; ++q) { y += rr[q].x; y += rr[q].y; y += rr[q].z; y += rr[q].w; }
-      y += v;
-      const int64_t row = r_begin + i;
-      if (p.bias) y += load_as_float_cg(p.bias, row, p.bias_dtype);
-      store_from_float(p.y, row * p.y_stride, p.y_dtype, y);
+  };
+  const uint8_t* ow_staged_rows = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);
+  if constexpr (NG == 1) {
+    final_rows(0, nrows, ow_staged, ow_staged_rows, 0, ow_ok);
+  } else if (!(kp.ow_ring_rows > 0 && p.n_out > 0)) {
+    final_rows(0, nrows, ow_staged, ow_staged_rows, 0, ow_ok);
+  } else {
+    // Two groups, outlier rows too large to stage: they stream through the
+    // ring once every stage is consumed (all its copies have landed: each was
+    // waited for), ow_ring_rows rows per piece by one bulk copy of the
+    // 16-byte-aligned middle plus plain loads of the ragged end.
+    const uint8_t* ow_src = reinterpret_cast<const uint8_t*>(p.ow);
+    uint8_t* ring = smem + kp.off_stage;
+    uint32_t ow_phase = 0;
+    for (int pr0 = 0; pr0 < nrows; pr0 += kp.ow_ring_rows) {  // CTA-uniform
+      const int pr1 = nrows - pr0 < kp.ow_ring_rows ? nrows : pr0 + kp.ow_ring_rows;
+      const int64_t pb0 = (r_begin + pr0) * row_bytes, pb1 = (r_begin + pr1) * row_bytes;
+      const int64_t pa0 = pb0 & ~int64_t(15);
+      const int64_t pa1 = (pb1 & ~int64_t(15)) > pa0 ? (pb1 & ~int64_t(15)) : pa0;
+      if (tid == 0) {
+        fence_proxy_async_smem();  // the ring's last reads were generic loads
+        mbar_arrive_expect_tx(&ow_bar, uint32_t(pa1 - pa0));
+        if (pa1 > pa0) bulk_g2s(ring, ow_src + pa0, uint32_t(pa1 - pa0), &ow_bar);
+      }
+      for (int64_t bt = pa1 + tid; bt < pb1; bt += kCT) ring[bt - pa0] = ow_src[bt];  // < 16 bytes
+      bool ok = mbar_wait_inl(&ow_bar, ow_phase, &s_abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) { s_abort = 1; atomicAdd(&g_gemv_pf_timeouts, 1); }
+      ow_phase ^= 1u;
+      compute_bar<kCT>();  // the plain tail stores
+      final_rows(pr0, pr1, true, ring + (pb0 - pa0), pr0, ow_ok && ok);
+      if (pr1 < nrows) compute_bar<kCT>();  // the next piece overwrites the ring
     }
   }
-  if (ow_ring && pr1 < nrows) compute_bar<kCT>();  // the next piece overwrites the ring
-  }  // pieces
 }
 
 inline size_t r16(size_t v) { return (v + 15) & ~size_t(15); }
