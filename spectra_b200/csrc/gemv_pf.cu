@@ -429,8 +429,9 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
         for (int h = 0; h < 2; ++h) {
           const float sa = __half2float(__ushort_as_half(uint16_t(scs[h] & 0xFFFFu)));
           const float sb = __half2float(__ushort_as_half(uint16_t(scs[h] >> 16)));
-          const float za = __uint_as_float((zrs[h] & 0xFFu) | kMagic) - 8388608.0f + 16.0f;
-          const float zb = __uint_as_float(((zrs[h] >> 8) & 0xFFu) | kMagic) - 8388608.0f + 16.0f;
+          // 2^23 + z (the zero-point byte under the exponent of 2^23) - (2^23 - 16) = 16 + z, exact
+          const float za = __uint_as_float(prmt(zrs[h], kMagic, 0x7540u)) - 8388592.0f;
+          const float zb = __uint_as_float(prmt(zrs[h], kMagic, 0x7541u)) - 8388592.0f;
           rs[h] = sa * fmaf(-za, XA, d[2 * h] + e[2 * h]) + sb * fmaf(-zb, XB, d[2 * h + 1] + e[2 * h + 1]);
         }
         acc0 += rs[0];
