@@ -35,7 +35,11 @@
 //   fills a ring of `ns` stages (every stage of the CTA up front when they fit)
 //   and refills it as stages free; the other warps compute: one group of 8,
 //   or two groups on alternate stages (whole-row-block stages: CTAs with >= 5
-//   row blocks; chunked stages: every CTA that owns its SM).
+//   row blocks; chunked stages: every CTA that owns its SM).  The CTA's
+//   outlier-weight rows arrive by one bulk copy before the wait when they
+//   fit beside a ring of >= 4 stages; otherwise (two groups only) they
+//   stream through the ring in pieces once its last stage is consumed, or
+//   (one group) are read from global memory in the final pass.
 //
 // Math (same as gemv.cu's tensor-core kernel)
 //   A unit is 16 rows x 8 groups (256 k).  Lane (g, c) of a warp holds rows g
