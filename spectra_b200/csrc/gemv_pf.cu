@@ -328,7 +328,9 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
     // Strided x: one pair per lane, 16 lanes per group.
     const int nstage = G * 16;
     const unsigned short* xh = reinterpret_cast<const unsigned short*>(p.x);
-    for (int e = tid; e < nstage; e += kCT) {  // nstage = 16 G, a multiple of kCT: uniform trip count
+    // nstage = 16 G = K / 2, a multiple of 256: the trip count is uniform
+    // within each warp (the shuffles below), not always across the CTA.
+    for (int e = tid; e < nstage; e += kCT) {
       const int gl = e >> 4, kk = e & 15;
       const int64_t kb = int64_t(gl) * kGroup;
       const uint32_t lo = __ldcg(xh + (kb + pair_k(kk, 0, p.layout)) * p.x_stride);

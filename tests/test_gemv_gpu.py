@@ -340,17 +340,21 @@ def test_gemv_prefetch_row_splits(N):
     assert_close_to_oracle(y, y_exact, y_round, od, f"N={N}")
 
 
-@pytest.mark.parametrize("K,N", [(8192, 148 * 16 * 5 + 7), (10240, 148 * 16 * 2 + 1), (5120, 148 * 16 * 5 + 3)])
-def test_gemv_prefetch_two_groups(K, N):
+@pytest.mark.parametrize("K,N,strided", [(8192, 148 * 16 * 5 + 7, False), (10240, 148 * 16 * 2 + 1, False),
+                                          (5120, 148 * 16 * 5 + 3, False), (3584, 148 * 16 * 5 + 9, True)])
+def test_gemv_prefetch_two_groups(K, N, strided):
     """Two compute groups on alternate stages: chunked stages for CTAs with
     >= 5 row blocks of a large K (ragged last block), an odd number of chunks
-    per row block, and whole-row-block stages whose ring depth (3) is rounded
-    down to an even number."""
+    per row block, whole-row-block stages whose ring depth (3) is rounded
+    down to an even number, and strided x (scalar staging whose trip count
+    differs between warps: K / 2 is not a multiple of the 512 threads)."""
     fmt = random_format(N, K, 9, seed=K + N)
     x = act(1, K, seed=K + N + 1, dtype="bf16")
+    if strided:  # a strided view on the device (a host copy would come back contiguous)
+        x = act(1, 2 * K, seed=K + N + 2, dtype="bf16").to(DEV)[:, ::2]
     y = out_f64(run_gemv(fmt, x)).reshape(-1)
-    y_exact, y_round, od = oracle_gemv(fmt, x)
-    assert_close_to_oracle(y, y_exact, y_round, od, f"{K}x{N}")
+    y_exact, y_round, od = oracle_gemv(fmt, x.cpu() if strided else x)
+    assert_close_to_oracle(y, y_exact, y_round, od, f"{K}x{N} strided={strided}")
 
 
 @pytest.mark.parametrize("n_out,ow_dt", [(601, "f32"), (700, "bf16")])
