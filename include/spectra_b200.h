@@ -183,6 +183,20 @@ SPECTRA_API int spectra_w4a16_gemm_noalloc(
     void* c, int c_dtype, int64_t c_row_stride,
     int64_t M, int64_t N, int64_t K, int layout, void* stream);
 
+/*
+ * Diagnostic, not a reference interface: the configuration the M=1 GEMV
+ * (spectra_w4a16_gemv) picks for contiguous, 16-byte-aligned weights of
+ * shape [N, K], contiguous x of x_dtype and n_out outlier columns of ow_dtype
+ * stored [N, n_out], on a GPU with `sms` SMs.  Computed on the host without a
+ * GPU.  out[10]: 1 if the weight-prefetching kernel takes the call (else all
+ * zero: the other kernel does), compute groups, chunked stages (1/0), ring
+ * stages, bytes per stage, outlier rows staged before the wait (1/0), outlier
+ * rows per piece streamed through the ring (0: none), dynamic shared memory
+ * bytes, grid, row blocks per CTA.
+ */
+SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_out, int x_dtype, int ow_dtype, int sms,
+                                     int64_t* out);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -613,39 +613,35 @@ bool encode_stage_maps(const GemvArgs& a, int kc, PfMaps<true>& maps) {
 
 }  // namespace
 
-int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
-  if (!pf_path_enabled()) return SPECTRA_ERR_UNSUPPORTED;
-  if (a.x_dtype != SPECTRA_DT_BF16 && a.x_dtype != SPECTRA_DT_F16) return SPECTRA_ERR_UNSUPPORTED;
-  if (a.K % kPfKQuantum != 0) return SPECTRA_ERR_UNSUPPORTED;
+// Kernel configuration of one call (with the PfParams it fills).
+struct PfPlan {
+  int ng = 0;            // compute groups
+  bool chunked = false;  // [16 x 2048] tensor-map stages (else whole row blocks)
+  int64_t grid = 0;
+  size_t smem = 0;       // dynamic shared memory bytes
+};
+
+// The configuration for `a` on a GPU with `sms` SMs, decided on the host
+// without any CUDA call (the caller encodes a chunked plan's tensor maps).
+// False: the prefetching kernel does not take this call.
+bool plan_gemv_pf(const GemvArgs& a, int sms, PfParams& kp, PfPlan& pl) {
+  if (a.x_dtype != SPECTRA_DT_BF16 && a.x_dtype != SPECTRA_DT_F16) return false;
+  if (a.K % kPfKQuantum != 0 || a.N <= 0 || sms <= 0) return false;
   const int G = a.K / kGroup;
-  if (!al16(a.packed) || !al16(a.scales) || !al16(a.zeros) || a.s_cs != 1 || a.z_cs != 1)
-    return SPECTRA_ERR_UNSUPPORTED;
+  if (!al16(a.packed) || !al16(a.scales) || !al16(a.zeros) || a.s_cs != 1 || a.z_cs != 1) return false;
   // Contiguous weights: a stage is a whole row block, three contiguous bulk
   // copies, when two such stages fit.  Otherwise stages of [16 rows x 2048
   // features] by tensor maps (row pitches must be multiples of 16 bytes).
   const bool contiguous = a.w_rs == a.K / 2 && a.s_rs == G && a.z_rs == G;
   const bool pitches16 = a.w_rs % 16 == 0 && (a.s_rs * 2) % 16 == 0 && a.z_rs % 16 == 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e);
-  if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
 
-  PfParams kp{};
+  kp = PfParams{};
   kp.a = a;
-  PfMaps<true> maps;
-  memset(&maps, 0, sizeof(maps));
   const int64_t nblk = (int64_t(a.N) + 15) / 16;
-  const int64_t grid = std::min<int64_t>(nblk, device_sms(dev));
+  const int64_t grid = std::min<int64_t>(nblk, sms);
   const int64_t rb_max = (nblk + grid - 1) / grid;
   kp.rows_max = int(rb_max * 16);
   kp.vec_x = (a.x_stride == 1 && al16(a.x)) ? 1 : 0;
-  // CTAs that own several row blocks run alone on their SM: sharing it with
-  // the next launch's prefetching CTA slowed a decoder layer by ~12 % (the
-  // co-resident copies delay this kernel's post-wait loads); CTAs with one
-  // row block finish quickly and keep the two-per-SM footprint.
-  const bool solo = rb_max > 1;
-  const size_t budget = solo ? kPfSmemSolo : kPfSmemPair;
-
   size_t off = 0;
   kp.off_x = 0;
   off = r16(size_t(G) * kXpWords * 4);
@@ -657,7 +653,14 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
 
   const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   const bool ow_contig = a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && al16(a.ow);
-  const bool bf = a.x_dtype == SPECTRA_DT_BF16;
+  // CTAs that own several row blocks run alone on their SM: sharing it with
+  // the next launch's prefetching CTA slowed a decoder layer by ~12 % (the
+  // co-resident copies delay this kernel's post-wait loads); CTAs with one
+  // row block finish quickly and keep the two-per-SM footprint -- unless that
+  // footprint cannot hold two stages (K = 28672: the staged x alone is 72 KB),
+  // then they own their SM too.
+  auto try_plan = [&](bool solo) -> bool {
+  const size_t budget = solo ? kPfSmemSolo : kPfSmemPair;
   // Whole-row-block stages unless a CTA owns >= 5 row blocks and the ring
   // holds fewer than kPfMinWholeStages of them: then the chunked mode's small
   // stages keep more copies in flight and feed two compute groups (8192 x
@@ -674,7 +677,6 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
     if (chunked && !pitches16) break;
     kp.kc = chunked ? std::min(a.K, kPfChunk) : a.K;
     kp.nkc = (a.K + kp.kc - 1) / kp.kc;
-    if (chunked && !encode_stage_maps(a, kp.kc, maps)) break;
     kp.off_sc = 16 * (kp.kc / 2);                    // codes [16][kc/2 B]
     kp.off_z = kp.off_sc + 16 * (kp.kc / 16);        // scales [16][kc/16 B]
     const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(kp.kc / kGroup));  // zero points [16][kc/32 B]
@@ -719,24 +721,92 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
           const int64_t rows = (ns * int64_t(sb) - 16) / row_bytes;
           if (rows >= rpp) kp.ow_ring_rows = int(std::min<int64_t>(kp.rows_max, rows - rows % rpp));
         }
-        size_t smem = size_t(kp.off_stage) + size_t(kp.ns) * sb;
-        if (solo) smem = std::max(smem, kPfSoloFloor);
-        if (chunked) {
-          if (ng == 2)
-            return bf ? launch_pf<true, 2, true>(maps, kp, grid, smem, dev, st)
-                      : launch_pf<false, 2, true>(maps, kp, grid, smem, dev, st);
-          return bf ? launch_pf<true, 1, true>(maps, kp, grid, smem, dev, st)
-                    : launch_pf<false, 1, true>(maps, kp, grid, smem, dev, st);
-        }
-        if (ng == 2)
-          return bf ? launch_pf<true, 2, false>(maps, kp, grid, smem, dev, st)
-                    : launch_pf<false, 2, false>(maps, kp, grid, smem, dev, st);
-        return bf ? launch_pf<true, 1, false>(maps, kp, grid, smem, dev, st)
-                  : launch_pf<false, 1, false>(maps, kp, grid, smem, dev, st);
+        pl.ng = ng;
+        pl.chunked = chunked != 0;
+        pl.grid = grid;
+        pl.smem = size_t(kp.off_stage) + size_t(kp.ns) * sb;
+        if (solo) pl.smem = std::max(pl.smem, kPfSoloFloor);
+        return true;
       }
     }
   }
-  return SPECTRA_ERR_UNSUPPORTED;
+  return false;
+  };
+  return try_plan(rb_max > 1) || (rb_max == 1 && try_plan(true));
+}
+
+int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
+  if (!pf_path_enabled()) return SPECTRA_ERR_UNSUPPORTED;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
+  PfParams kp{};
+  PfPlan pl;
+  if (!plan_gemv_pf(a, device_sms(dev), kp, pl)) return SPECTRA_ERR_UNSUPPORTED;
+  PfMaps<true> maps;
+  memset(&maps, 0, sizeof(maps));
+  if (pl.chunked && !encode_stage_maps(a, kp.kc, maps)) return SPECTRA_ERR_UNSUPPORTED;
+  const bool bf = a.x_dtype == SPECTRA_DT_BF16;
+  if (pl.chunked) {
+    if (pl.ng == 2)
+      return bf ? launch_pf<true, 2, true>(maps, kp, pl.grid, pl.smem, dev, st)
+                : launch_pf<false, 2, true>(maps, kp, pl.grid, pl.smem, dev, st);
+    return bf ? launch_pf<true, 1, true>(maps, kp, pl.grid, pl.smem, dev, st)
+              : launch_pf<false, 1, true>(maps, kp, pl.grid, pl.smem, dev, st);
+  }
+  if (pl.ng == 2)
+    return bf ? launch_pf<true, 2, false>(maps, kp, pl.grid, pl.smem, dev, st)
+              : launch_pf<false, 2, false>(maps, kp, pl.grid, pl.smem, dev, st);
+  return bf ? launch_pf<true, 1, false>(maps, kp, pl.grid, pl.smem, dev, st)
+            : launch_pf<false, 1, false>(maps, kp, pl.grid, pl.smem, dev, st);
 }
 
 }  // namespace spectra
+
+// Diagnostic (declared in include/spectra_b200.h): the plan above for
+// contiguous, 16-byte-aligned weights, contiguous x and [N, n_out] outlier
+// weights, without a GPU.
+extern "C" SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_out, int x_dtype, int ow_dtype,
+                                                int sms, int64_t* out) {
+  if (!out) return SPECTRA_ERR_NULL_POINTER;
+  if (N <= 0 || K <= 0 || K % 32 != 0 || n_out < 0 || n_out > K || N > 2147483647LL || K > 2147483647LL)
+    return SPECTRA_ERR_SHAPE;
+  spectra::GemvArgs a{};
+  const uintptr_t aligned = 4096;  // stand-in 16-byte-aligned addresses (never dereferenced)
+  a.x = reinterpret_cast<const void*>(aligned);
+  a.x_dtype = x_dtype;
+  a.x_stride = 1;
+  a.packed = reinterpret_cast<const uint8_t*>(aligned);
+  a.w_rs = K / 2;
+  a.scales = reinterpret_cast<const __half*>(aligned);
+  a.s_rs = K / 32;
+  a.s_cs = 1;
+  a.zeros = reinterpret_cast<const uint8_t*>(aligned);
+  a.z_rs = K / 32;
+  a.z_cs = 1;
+  a.n_out = int(n_out);
+  a.ow = n_out > 0 ? reinterpret_cast<const void*>(aligned) : nullptr;
+  a.ow_dtype = ow_dtype;
+  a.ow_rs = n_out;
+  a.ow_cs = 1;
+  a.N = int(N);
+  a.K = int(K);
+  a.layout = SPECTRA_LAYOUT_MARLIN;
+  spectra::PfParams kp{};
+  spectra::PfPlan pl;
+  const bool taken = spectra::plan_gemv_pf(a, sms, kp, pl);
+  for (int i = 0; i < 10; ++i) out[i] = 0;
+  if (!taken) return SPECTRA_OK;
+  out[0] = 1;
+  out[1] = pl.ng;
+  out[2] = pl.chunked ? 1 : 0;
+  out[3] = kp.ns;
+  out[4] = kp.stage_bytes;
+  out[5] = kp.off_ow >= 0 ? 1 : 0;
+  out[6] = kp.ow_ring_rows;
+  out[7] = int64_t(pl.smem);
+  out[8] = pl.grid;
+  out[9] = kp.rows_max / 16;
+  return SPECTRA_OK;
+}

@@ -341,13 +341,15 @@ def test_gemv_prefetch_row_splits(N):
 
 
 @pytest.mark.parametrize("K,N,strided", [(8192, 148 * 16 * 5 + 7, False), (10240, 148 * 16 * 2 + 1, False),
-                                          (5120, 148 * 16 * 5 + 3, False), (3584, 148 * 16 * 5 + 9, True)])
+                                          (5120, 148 * 16 * 5 + 3, False), (3584, 148 * 16 * 5 + 9, True),
+                                          (28672, 1024, False)])
 def test_gemv_prefetch_two_groups(K, N, strided):
     """Two compute groups on alternate stages: chunked stages for CTAs with
     >= 5 row blocks of a large K (ragged last block), an odd number of chunks
     per row block, whole-row-block stages whose ring depth (3) is rounded
-    down to an even number, and strided x (scalar staging whose trip count
-    differs between warps: K / 2 is not a multiple of the 512 threads)."""
+    down to an even number, strided x (scalar staging whose trip count
+    differs between warps: K / 2 is not a multiple of the 512 threads), and
+    one row block per CTA at K = 28672 (the CTA owns its SM)."""
     fmt = random_format(N, K, 9, seed=K + N)
     x = act(1, K, seed=K + N + 1, dtype="bf16")
     if strided:  # a strided view on the device (a host copy would come back contiguous)
