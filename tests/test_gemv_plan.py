@@ -71,8 +71,8 @@ def test_plan_invariants(K, N, n_out, ow):
     n_out = min(n_out, K)
     p = plan(N, K, n_out, ow=ow)
     if not p["taken"]:
-        # e.g. K = 28672 with one row block per CTA: the staged x leaves one
-        # chunk stage in a two-per-SM CTA; the register-prefetch kernel runs
+        # e.g. K = 57344 with 55 row blocks per CTA: the staged x (143 KB) and
+        # the row partials leave one chunk stage; the register-prefetch kernel runs
         assert all(v == 0 for v in p.values())
         return
     nblk = (N + 15) // 16
