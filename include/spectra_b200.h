@@ -166,7 +166,10 @@ SPECTRA_API size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int6
  *     zero again, so the caller never clears anything.
  *   - Setup: the first call on each device looks the array's address up with
  *     cudaGetSymbolAddress (with that device current), which may load the
- *     module; make that first call before any stream capture begins.
+ *     module; make that first call before any stream capture begins.  The
+ *     address is looked up again when the device's context has been recreated
+ *     since (cudaDeviceReset), so make the first call after a reset outside a
+ *     capture too.
  *   - Races: all calls on one device (all streams and host threads of the
  *     process) share the one array, so calls that overlap in time race and
  *     give wrong results.  Issue them one after another, e.g. on one stream.
@@ -182,6 +185,29 @@ SPECTRA_API int spectra_w4a16_gemm_noalloc(
     const void* outlier_w, int ow_dtype, int64_t ow_row_stride, int64_t ow_col_stride,
     void* c, int c_dtype, int64_t c_row_stride,
     int64_t M, int64_t N, int64_t K, int layout, void* stream);
+
+/*
+ * Diagnostic, not a reference interface (the reference's Triton kernels have
+ * no bounded waits).  Every pipeline wait in this library's kernels gives up
+ * after 2 s instead of hanging; the kernel then abandons its work, leaves the
+ * output of that call undefined and counts the event in a device counter.
+ * This returns in *count the number of such timed-out waits on the current
+ * device since the library loaded (or since the last reset), and zeroes the
+ * counters if `reset` is non-zero.  It reads device memory, so it waits for
+ * all work queued on the device: call it between steps, not inside a CUDA
+ * graph capture.  A non-zero count means the results of some earlier call
+ * must be discarded.
+ */
+SPECTRA_API int spectra_device_timeouts(int64_t* count, int reset);
+
+/*
+ * Self-test of the bounded wait (not a reference interface): launches one
+ * thread that waits on a pipeline barrier nothing ever arrives on.  The wait
+ * gives up after the library's 2 s limit, the kernel returns and
+ * spectra_device_timeouts() counts one more timeout.  Nothing is copied and
+ * nothing is written besides the counter.
+ */
+SPECTRA_API int spectra_selftest_wait_timeout(void* stream);
 
 /*
  * Diagnostic, not a reference interface: the configuration the M=1 GEMV

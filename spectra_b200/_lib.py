@@ -56,6 +56,8 @@ PROTOTYPES = {
         c_void_p, c_int, c_int64,                      # c, c_dtype, c_row_stride
         c_int64, c_int64, c_int64, c_int,              # M, N, K, layout
         c_void_p]),                                    # stream
+    "spectra_device_timeouts": (c_int, [c_void_p, c_int]),
+    "spectra_selftest_wait_timeout": (c_int, [c_void_p]),
     "spectra_w4a16_dequant": (c_int, [
         c_void_p, c_int64,
         c_void_p, c_int64, c_int64,

@@ -1,6 +1,8 @@
 // extern "C" entry points of libspectra_b200.so (declared in
 // include/spectra_b200.h).  Every argument check runs on the host before any
 // CUDA call, so an invalid call returns a status code and launches nothing.
+#include <cuda.h>
+
 #include <cstdint>
 #include <cstdlib>
 
@@ -31,6 +33,28 @@ int check_weights(const uint8_t* packed, const uint16_t* scales, const uint8_t* 
 }  // namespace
 
 void set_last_cuda_error(cudaError_t e) { g_last_cuda_error = int(e); }
+
+namespace {
+void* driver_entry(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return p;
+}
+}  // namespace
+
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static const GetCurrent get_current = reinterpret_cast<GetCurrent>(driver_entry("cuCtxGetCurrent"));
+  static const GetId get_id = reinterpret_cast<GetId>(driver_entry("cuCtxGetId"));
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
 
 bool pdl_enabled() {
   static const bool on = [] {
@@ -208,6 +232,19 @@ int spectra_w4a16_gemm_noalloc(
                             ow_row_stride, ow_col_stride, c, c_dtype, c_row_stride, M, N, K, layout, scratch,
                             scratch_bytes, stream);
 }
+
+int spectra_device_timeouts(int64_t* count, int reset) {
+  if (!count) return SPECTRA_ERR_NULL_POINTER;
+  long long a = 0, b = 0, c = 0;
+  int st = gemv_timeouts(&a, reset != 0);
+  if (st == SPECTRA_OK) st = gemv_pf_timeouts(&b, reset != 0);
+  if (st == SPECTRA_OK) st = gemm_timeouts(&c, reset != 0);
+  if (st != SPECTRA_OK) return st;
+  *count = int64_t(a + b + c);
+  return SPECTRA_OK;
+}
+
+int spectra_selftest_wait_timeout(void* stream) { return launch_selftest_wait(static_cast<cudaStream_t>(stream)); }
 
 size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "spectra_b200.h"
 
 namespace spectra {
@@ -43,6 +45,55 @@ inline int cuda_status(cudaError_t e) {
   }
   return SPECTRA_OK;
 }
+
+// Unique id of the CUDA context current on the calling thread (0: none yet).
+// A device's primary context gets a new id when it is torn down and created
+// again (cudaDeviceReset), which invalidates everything cached per device:
+// kernel attributes and module symbol addresses.
+unsigned long long current_context_id();
+
+// One-time initialisation per (device, CUDA context): `init` runs on the first
+// call on each device and again after that device's context was recreated.
+// Two host threads making their first call at once may both run `init`, so it
+// must be idempotent (setting a kernel attribute, looking an address up).
+class PerContextOnce {
+ public:
+  template <class F>
+  cudaError_t run(int dev, F&& init) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    const unsigned long long id = current_context_id();
+    if (id != 0 && ctx_[dev].load(std::memory_order_acquire) == id) return cudaSuccess;
+    const cudaError_t e = init();  // a runtime call: makes the primary context current
+    if (e == cudaSuccess) ctx_[dev].store(current_context_id(), std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::atomic<unsigned long long> ctx_[kMaxDevices] = {};
+};
+
+// Reads a device-side counter of waits that gave up (a `__device__ int` of the
+// calling translation unit) on the current device, and zeroes it if `reset`.
+// Synchronous: it waits for the device's queued work.
+template <class T>
+int read_timeout_counter(const T& symbol, long long* out, bool reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, symbol, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(symbol, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return cuda_status(e);
+  *out = v;
+  return SPECTRA_OK;
+}
+
+// Timed-out waits counted by each kernel family (per translation unit).
+int gemv_timeouts(long long* out, bool reset);
+int gemv_pf_timeouts(long long* out, bool reset);
+int gemm_timeouts(long long* out, bool reset);
+// Launches the bounded-wait self-test kernel (gemv_pf.cu).
+int launch_selftest_wait(cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // typed scalar loads/stores selected by a runtime dtype code

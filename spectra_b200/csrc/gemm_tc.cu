@@ -888,12 +888,9 @@ int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmK
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   if (dev < 0 || dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  static bool attr_set[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem));
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[dev] = true;
-  }
+  static PerContextOnce attrs;
+  e = attrs.run(dev, [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem)); });
+  if (e != cudaSuccess) return cuda_status(e);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(pl.tiles_n * pl.S), unsigned(pl.m_chunks));
   cfg.blockDim = dim3(kThreads);
@@ -987,20 +984,30 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
 }
 
 int gemm_noalloc_scratch(void** ptr, size_t* bytes) {
+  // The array's device address, looked up once per device and again whenever
+  // that device's context was recreated (cudaDeviceReset reloads the module,
+  // and the array may then live elsewhere).  The address is stored before the
+  // context id, so a reader that sees its own context's id reads its address.
+  static std::atomic<unsigned long long> ctx_of[kMaxDevices];
   static std::atomic<void*> addr[kMaxDevices];
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   if (dev < 0 || dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  void* p = addr[dev].load(std::memory_order_acquire);
+  const unsigned long long id = current_context_id();
+  void* p = nullptr;
+  if (id != 0 && ctx_of[dev].load(std::memory_order_acquire) == id) p = addr[dev].load(std::memory_order_acquire);
   if (p == nullptr) {
-    e = cudaGetSymbolAddress((void**)&p, g_gemm_noalloc_scratch);
+    e = cudaGetSymbolAddress((void**)&p, g_gemm_noalloc_scratch);  // with `dev` current
     if (e != cudaSuccess) return cuda_status(e);
     addr[dev].store(p, std::memory_order_release);
+    ctx_of[dev].store(current_context_id(), std::memory_order_release);
   }
   *ptr = p;
   *bytes = sizeof(g_gemm_noalloc_scratch);
   return SPECTRA_OK;
 }
+
+int gemm_timeouts(long long* out, bool reset) { return read_timeout_counter(g_gemm_timeouts, out, reset); }
 
 }  // namespace spectra

@@ -416,13 +416,9 @@ int launch_rows(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  static bool attr_set[kMaxDevices] = {};
-  static int occ[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemvMaxSmem));
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[dev] = true;
-  }
+  static PerContextOnce attrs;
+  e = attrs.run(dev, [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemvMaxSmem)); });
+  if (e != cudaSuccess) return cuda_status(e);
   const GemvArgs& a = kp.a;
   auto r16 = [](size_t v) { return (v + 15) & ~size_t(15); };
   const int G = a.K / kGroup;
@@ -450,7 +446,6 @@ int launch_rows(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
     }
   }
   if (smem > kGemvMaxSmem) return SPECTRA_ERR_UNSUPPORTED;
-  (void)occ;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
@@ -760,12 +755,9 @@ int launch_mma(GemvKParams kp, const GemvPlan& pl, cudaStream_t st) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   if (dev >= kMaxDevices) return SPECTRA_ERR_UNSUPPORTED;
-  static bool attr_set[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemvMaxSmem));
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[dev] = true;
-  }
+  static PerContextOnce attrs;
+  e = attrs.run(dev, [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemvMaxSmem)); });
+  if (e != cudaSuccess) return cuda_status(e);
   const GemvArgs& a = kp.a;
   auto r16 = [](size_t v) { return (v + 15) & ~size_t(15); };
   const int G = a.K / kGroup;
@@ -856,5 +848,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   if (align == 4) return launch_rows_align<4>(kp, pl, st);
   return launch_rows_align<1>(kp, pl, st);
 }
+
+int gemv_timeouts(long long* out, bool reset) { return read_timeout_counter(g_gemv_timeouts, out, reset); }
 
 }  // namespace spectra

@@ -558,6 +558,24 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   }
 }
 
+// Self-test of the bounded wait: one thread waits on an mbarrier phase that
+// never completes (nothing arrives on it), with the production limit of
+// sm100::kWaitLimitNs.  The wait gives up, the timeout is counted exactly as
+// the pipeline kernels count theirs, and the kernel returns; no copy is in
+// flight at any point.
+__global__ void selftest_wait_kernel() {
+  using namespace sm100;
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0u, &s_abort)) atomicAdd(&g_gemv_pf_timeouts, 1);
+}
+
 inline size_t r16(size_t v) { return (v + 15) & ~size_t(15); }
 inline size_t r128(size_t v) { return (v + 127) & ~size_t(127); }
 inline bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
@@ -565,14 +583,14 @@ inline bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) 
 template <bool BF16, int NG, bool CHUNKED>
 int launch_pf(const PfMaps<true>& all_maps, const PfParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
   auto kern = gemv_pf_kernel<BF16, NG, CHUNKED>;
-  static bool attr_set[kMaxDevices] = {};
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmemSolo));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[dev] = true;
-  }
+  static PerContextOnce attrs;
+  cudaError_t e = attrs.run(dev, [&] {
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPfSmemSolo));
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    return r;
+  });
+  if (e != cudaSuccess) return cuda_status(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3((NG * kPfGroupWarps + 1) * 32);
@@ -735,6 +753,13 @@ bool plan_gemv_pf(const GemvArgs& a, int sms, PfParams& kp, PfPlan& pl) {
   return try_plan(rb_max > 1) || (rb_max == 1 && try_plan(true));
 }
 
+int gemv_pf_timeouts(long long* out, bool reset) { return read_timeout_counter(g_gemv_pf_timeouts, out, reset); }
+
+int launch_selftest_wait(cudaStream_t st) {
+  selftest_wait_kernel<<<1, 32, 0, st>>>();
+  return cuda_status(cudaGetLastError());
+}
+
 int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
   if (!pf_path_enabled()) return SPECTRA_ERR_UNSUPPORTED;
   int dev = 0;
@@ -772,6 +797,9 @@ extern "C" SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_
   if (!out) return SPECTRA_ERR_NULL_POINTER;
   if (N <= 0 || K <= 0 || K % 32 != 0 || n_out < 0 || n_out > K || N > 2147483647LL || K > 2147483647LL)
     return SPECTRA_ERR_SHAPE;
+  // the dtype codes spectra_w4a16_gemv accepts (x: F16|BF16|F32; outlier weights: F16|BF16|F32)
+  auto float_dt = [](int dt) { return dt == SPECTRA_DT_F16 || dt == SPECTRA_DT_BF16 || dt == SPECTRA_DT_F32; };
+  if (!float_dt(x_dtype) || (n_out > 0 && !float_dt(ow_dtype))) return SPECTRA_ERR_DTYPE;
   spectra::GemvArgs a{};
   const uintptr_t aligned = 4096;  // stand-in 16-byte-aligned addresses (never dereferenced)
   a.x = reinterpret_cast<const void*>(aligned);

@@ -140,17 +140,33 @@ def fused_w4a16_gemv_hdsq(
 
 # Split-K workspace, one per (device, stream): calls that share one must not
 # overlap in time, and calls on one stream never do.  Zeroed when allocated;
-# every GEMM call leaves its counters zero again.
+# every GEMM call leaves its counters zero again.  A workspace that grows is
+# replaced, but the old buffer is kept alive: a CUDA graph captured earlier on
+# the same stream still holds its address, and replaying that graph must not
+# write into memory the caching allocator has handed to another tensor.
 _WORKSPACES: dict = {}
+_RETIRED_WORKSPACES: list = []
 
 
 def _workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     key = (dev.index, stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _RETIRED_WORKSPACES.append(ws)
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
         _WORKSPACES[key] = ws
     return ws
+
+
+def device_timeouts(reset: bool = False) -> int:
+    """Pipeline waits that gave up (2 s limit) in this library's kernels on the
+    current device since load or the last reset.  Synchronises the device.  A
+    non-zero count means the outputs of the calls that timed out are undefined."""
+    import ctypes
+    n = ctypes.c_int64(0)
+    L.check("spectra_device_timeouts", L.lib().spectra_device_timeouts(ctypes.byref(n), int(reset)))
+    return int(n.value)
 
 
 def batched_w4a16_gemm(
@@ -192,7 +208,14 @@ def batched_w4a16_gemm(
     if a2.stride(1) != 1 or (a2.stride(0) * 2) % 16 or a2.data_ptr() % 16 or a2.stride(0) < K:
         a2 = a2.clone(memory_format=torch.contiguous_format)
     if packed.data_ptr() % 16 or packed.stride(0) % 16:
-        packed = packed.clone(memory_format=torch.contiguous_format)
+        # The tensor-core GEMM streams weight rows by TMA, which needs a 16-byte
+        # aligned base and row pitch.  Copying the weights here would double
+        # the call's traffic, silently and on every call, so such views are
+        # rejected; the M=1 GEMV accepts them.
+        raise ValueError(
+            "batched_w4a16_gemm: packed weights need a 16-byte aligned base address and row stride "
+            f"(got address % 16 = {packed.data_ptr() % 16}, row stride {packed.stride(0)} bytes); "
+            "pass a contiguous or 16-byte-aligned view")
     layout = L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD
     lib = L.lib()
     with torch.cuda.device(dev):

@@ -42,7 +42,10 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("SPECTRA_REF", "/root/reference")
+REF = os.environ.get("SPECTRA_REF")
+if not REF:
+    sys.exit("make_golden.py: set SPECTRA_REF to the root of a NeuraCryption/SPECTRA checkout "
+             "(the directory that holds spectra/compressor.py and spectra/kernels.py)")
 sys.path.insert(0, REF)
 
 from spectra.compressor import SpectraCompressor  # noqa: E402

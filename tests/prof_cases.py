@@ -1,7 +1,7 @@
 """Minimal drivers for profiling one kernel shape under ncu.
 
-    python -m spectra_b200.prof gemv K N n_out iters [--dtype bf16|f16]
-    python -m spectra_b200.prof gemm M K N n_out iters [--dtype bf16|f16]
+    python -m tests.prof_cases gemv K N n_out iters [--dtype bf16|f16]
+    python -m tests.prof_cases gemm M K N n_out iters [--dtype bf16|f16]
 
 Builds random tensors in SPECTRA's weight format of that shape on cuda:0
 (codes uniform 0..15, fp16 scales in the range the compressor produces for

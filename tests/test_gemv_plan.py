@@ -114,3 +114,14 @@ def test_bad_arguments():
     assert f(16, 2000, 0, BF16, F16, SMS, out) == 2     # K not a multiple of 32
     assert f(16, 2048, 4096, BF16, F16, SMS, out) == 2  # more outlier columns than features
     assert f(16, 2048, 0, BF16, F16, SMS, None) == 1    # SPECTRA_ERR_NULL_POINTER
+
+
+@pytest.mark.parametrize("ow_dtype", [3, 4, 9, -1])  # I32, I64, unknown codes
+def test_unknown_outlier_weight_dtype_is_rejected_like_the_gemv(ow_dtype):
+    # spectra_w4a16_gemv rejects these with SPECTRA_ERR_DTYPE, so the diagnostic must too
+    f = _fn()
+    out = (ctypes.c_int64 * 10)()
+    assert f(4096, 4096, 41, BF16, ow_dtype, SMS, out) == 5  # SPECTRA_ERR_DTYPE
+    assert f(4096, 4096, 41, 7, F16, SMS, out) == 5          # unknown x dtype
+    # without outlier columns the outlier dtype is not looked at (as in the GEMV)
+    assert f(4096, 4096, 0, BF16, ow_dtype, SMS, out) == 0
