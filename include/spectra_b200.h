@@ -187,6 +187,101 @@ SPECTRA_API int spectra_w4a16_gemm_noalloc(
     int64_t M, int64_t N, int64_t K, int layout, void* stream);
 
 /*
+ * Group-32 INT4 quantiser on the GPU: the tensors SpectraCompressor writes
+ * for one weight (replaces SpectraCompressor._quantize_chunk_group32 and
+ * _compute_group32_quant, spectra/compressor.py:72-156).  Input columns listed
+ * in outlier_idx (may be NULL with n_out = 0) are read as zero, as the
+ * reference zeroes them before quantising (:137-140).  Per group of 32: fp32
+ * min/max, s = (max-min)/15 (constant groups: |min|, or 1 when min == 0),
+ * clamped to >= 1e-8, z = clamp(round(-min/s), 0, 15), q = clamp(round((w +
+ * z*s)/s), 0, 15), round half to even, correctly rounded divisions: the codes
+ * are bit-identical to the reference run on a CPU.
+ *   w       [N, K] at w + n*w_row_stride + k, w_dtype F16|BF16|F32
+ *   packed  [N, K/2] (layout MARLIN as the compressor writes, or EVEN_ODD)
+ *   scales  [N, K/32] fp16 bits
+ *   zeros   [N, K/32] one byte per group (as the engine binds them) or NULL
+ *   packed_zeros [N, ceil(K/64)] two per byte, low nibble = even group (the
+ *           container form, spectra/compressor.py:104-110) or NULL
+ */
+SPECTRA_API int spectra_quantize_group32(
+    const void* w, int w_dtype, int64_t w_row_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    uint8_t* packed, int64_t p_row_stride,
+    uint16_t* scales, int64_t s_row_stride,
+    uint8_t* zeros, int64_t z_row_stride,
+    uint8_t* packed_zeros, int64_t pz_row_stride,
+    int64_t N, int64_t K, int layout, void* stream);
+
+/*
+ * Load-time zero-point unpack on the GPU (replaces the torch code at
+ * spectra/engine.py:1007-1012): packed_zeros [N, ceil(G/2)] (low nibble =
+ * group 2j, high nibble = group 2j+1) -> zeros [N, G], one byte per group.
+ */
+SPECTRA_API int spectra_unpack_zeros(const uint8_t* packed_zeros, int64_t pz_row_stride, uint8_t* zeros,
+                                     int64_t z_row_stride, int64_t N, int64_t G, void* stream);
+
+/*
+ * INT4 KV-cache quantiser (replaces SpectraGroup32QuantizedLayer._quantize,
+ * spectra/engine.py:625-656).  t: contiguous [rows, D] F16|BF16; groups of 32
+ * along D (zero-padded to a multiple of 32, G = ceil(D/32)); computed in t's
+ * dtype with the reference's rounding steps as torch runs them on a CUDA
+ * device.  Outputs (contiguous): packed [rows, G, 16] even-odd nibbles
+ * (16-byte aligned), scales [rows, G] fp16 bits, zeros [rows, G] bytes.
+ */
+SPECTRA_API int spectra_kv_quantize(const void* t, int t_dtype, int64_t rows, int64_t D, uint8_t* packed,
+                                    uint16_t* scales, uint8_t* zeros, void* stream);
+
+/*
+ * INT4 KV-cache dequantiser (replaces SpectraGroup32QuantizedLayer._dequantize,
+ * spectra/engine.py:658-671): out [rows, D] = (q - z) * s, exact in fp32,
+ * rounded once to out_dtype (the reference returns bf16); padding dropped.
+ */
+SPECTRA_API int spectra_kv_dequantize(const uint8_t* packed, const uint16_t* scales, const uint8_t* zeros,
+                                      void* out, int out_dtype, int64_t rows, int64_t D, void* stream);
+
+/*
+ * Quantised token-embedding gather (replaces SpectraFusedEmbedding.forward,
+ * spectra/engine.py:167-212): out[t, :] = dequantised row ids[t] of the
+ * [V, K] vocabulary matrix ((q - z) * s in fp32, rounded once to out_dtype),
+ * then the outlier columns set to outlier_w[ids[t], j] rounded to out_dtype.
+ * zeros_packed != 0: zeros are [V, ceil(G/2)] two per byte.  An id outside
+ * [0, V) yields a zero row.
+ *   ids    [T] I32|I64;  packed [V, K/2];  scales [V, K/32] fp16 bits
+ *   outlier_w [v, j] at outlier_w + v*ow_row_stride + j
+ *   out    [T, K] at out + t*out_row_stride + k, out_dtype F16|BF16|F32
+ */
+SPECTRA_API int spectra_w4a16_embedding(
+    const void* ids, int ids_dtype, int64_t T,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int zeros_packed,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride,
+    void* out, int out_dtype, int64_t out_row_stride,
+    int64_t V, int64_t K, int layout, void* stream);
+
+/*
+ * Greedy next-token choice (the argmax of the engine's temperature-0
+ * sample_token, spectra/engine.py:1690-1713): idx[m] = idx_offset + the first
+ * index of the maximum of row m of x [M, N] (a NaN counts as the maximum, as
+ * in torch.argmax); val[m] (optional) = that maximum as fp32.  idx_offset lets
+ * an N-sharded lm_head report the layer's row index, so the shards reduce
+ * (value, index) pairs instead of gathering every logit.
+ */
+SPECTRA_API int spectra_argmax(const void* x, int x_dtype, int64_t x_row_stride, int64_t M, int64_t N,
+                               int64_t idx_offset, int64_t* idx, float* val, void* stream);
+
+/*
+ * Walsh-Hadamard rotation of activation rows, the optional GEMV prologue
+ * (the reference's fast_walsh_hadamard_transform, spectra/compressor.py:29-42,
+ * which its compressor cannot yet apply to weights: off by default in the
+ * drop-in).  y[m] = H x[m] (/ sqrt(n) if normalize), butterflies in fp32, one
+ * rounding to y_dtype; n a power of two, <= 32768.
+ */
+SPECTRA_API int spectra_fwht(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,
+                             int64_t y_row_stride, int64_t M, int64_t n, int normalize, void* stream);
+
+/*
  * Diagnostic, not a reference interface (the reference's Triton kernels have
  * no bounded waits).  Every pipeline wait in this library's kernels gives up
  * after 2 s instead of hanging; the kernel then abandons its work, leaves the

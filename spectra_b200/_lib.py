@@ -56,6 +56,25 @@ PROTOTYPES = {
         c_void_p, c_int, c_int64,                      # c, c_dtype, c_row_stride
         c_int64, c_int64, c_int64, c_int,              # M, N, K, layout
         c_void_p]),                                    # stream
+    "spectra_quantize_group32": (c_int, [
+        c_void_p, c_int, c_int64,                      # w, w_dtype, w_row_stride
+        c_void_p, c_int, c_int64,                      # outlier_idx, idx_dtype, n_out
+        c_void_p, c_int64, c_void_p, c_int64,          # packed, scales
+        c_void_p, c_int64, c_void_p, c_int64,          # zeros, packed_zeros
+        c_int64, c_int64, c_int, c_void_p]),           # N, K, layout, stream
+    "spectra_unpack_zeros": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "spectra_kv_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "spectra_kv_dequantize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p]),
+    "spectra_w4a16_embedding": (c_int, [
+        c_void_p, c_int, c_int64,                      # ids, ids_dtype, T
+        c_void_p, c_int64, c_void_p, c_int64,          # packed, scales
+        c_void_p, c_int64, c_int,                      # zeros, z_row_stride, zeros_packed
+        c_void_p, c_int, c_int64,                      # outlier_idx, idx_dtype, n_out
+        c_void_p, c_int, c_int64,                      # outlier_w, ow_dtype, ow_row_stride
+        c_void_p, c_int, c_int64,                      # out, out_dtype, out_row_stride
+        c_int64, c_int64, c_int, c_void_p]),           # V, K, layout, stream
+    "spectra_argmax": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "spectra_fwht": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p]),
     "spectra_device_timeouts": (c_int, [c_void_p, c_int]),
     "spectra_selftest_wait_timeout": (c_int, [c_void_p]),
     "spectra_w4a16_dequant": (c_int, [

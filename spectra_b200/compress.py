@@ -1,21 +1,22 @@
 """Device-side weight compressor: the tensors SPECTRA's compressor writes for
-one linear layer, produced with torch ops on whatever device the weight lives
-on (a CUDA device in the bench, the CPU in the tests).
+one linear layer, produced on the GPU.
 
 It restates, in its own code, the algorithm of ``SpectraCompressor``:
-  * group-32 asymmetric min/max INT4 codes (spectra/compressor.py:72-112):
-    s = (max-min)/15 (constant groups: |min| or 1), z = clamp(round(-min/s)),
-    q = clamp(round((w + z*s)/s)), fp32 arithmetic, round-half-to-even;
-    Marlin packing (k in the low nibble, k+16 in the high nibble);
+  * group-32 asymmetric min/max INT4 codes (spectra/compressor.py:72-156):
+    the CUDA kernel ``spectra_quantize_group32`` (csrc/format.cu) -- fp32
+    arithmetic in the reference's operation order, round half to even,
+    correctly rounded divisions, Marlin packing; bit-identical to the
+    reference run on a CPU;
   * kurtosis-adaptive outlier columns (spectra/compressor.py:158-215): fp32
     column L2 norms, ratio = clamp(0.01*(1+0.15*log1p(max(0, kurt-3))),
     0.005, 0.03), top-k columns sorted ascending, zeroed before quantisation
-    and kept exactly in the source dtype;
-  * the load-time zero-point unpack (spectra/engine.py:1007-1012).
-Every elementwise step is an IEEE fp32 operation in the same order as the
-reference, so codes, scales and zero points are bit-identical to it; only
-the column-norm reduction order can differ, which matters only for exact
-near-ties between column norms.
+    and kept exactly in the source dtype (torch reductions on the device:
+    a K-long vector, not the hot path);
+  * the load-time zero-point unpack (spectra/engine.py:1007-1012): the CUDA
+    kernel ``spectra_unpack_zeros``.
+The kernels need CUDA tensors; there is no CPU path (the numpy restatement in
+``oracle/`` is the checker).  Only the column-norm reduction order can differ
+from the reference, which matters only for exact near-ties between norms.
 """
 from __future__ import annotations
 
@@ -25,7 +26,12 @@ from typing import Optional
 
 import torch
 
+from . import _lib as L
+
 GROUP = 32
+
+_DT = {torch.float16: L.DT_F16, torch.bfloat16: L.DT_BF16, torch.float32: L.DT_F32,
+       torch.int32: L.DT_I32, torch.int64: L.DT_I64}
 
 
 @dataclass
@@ -40,42 +46,72 @@ class CompressedLinear:
     kurtosis: float
 
 
-def quantize_group32(w: torch.Tensor):
-    """Group-32 INT4 codes of ``w`` [N, K] (any float dtype).
+def _cuda(name: str, t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"spectra_b200.compress: {name} must be a CUDA tensor (no CPU path), got {t.device}")
 
-    Returns (packed u8 [N,K/2], scales fp16 [N,K/32], packed_zeros u8 [N,ceil(G/2)]).
+
+def quantize_group32(w: torch.Tensor, outlier_idx: Optional[torch.Tensor] = None, marlin_layout: bool = True):
+    """Group-32 INT4 codes of ``w`` [N, K] (fp16/bf16/fp32, CUDA), columns in
+    ``outlier_idx`` read as zero.
+
+    Returns (packed u8 [N,K/2], scales fp16 [N,K/32], zeros u8 [N,K/32],
+    packed_zeros u8 [N,ceil(G/2)]).
     """
+    _cuda("w", w)
+    if w.dim() != 2 or w.shape[1] % GROUP:
+        raise ValueError("w must be [N, K] with K a multiple of 32")
+    if w.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise TypeError(f"unsupported weight dtype {w.dtype}")
+    if w.stride(1) != 1:
+        w = w.contiguous()
     N, K = w.shape
-    if K % GROUP:
-        raise ValueError("K must be a multiple of 32")
     G = K // GROUP
-    wg = w.reshape(N, G, GROUP).to(torch.float32)
-    lo = wg.amin(dim=-1, keepdim=True)
-    hi = wg.amax(dim=-1, keepdim=True)
-    span = hi - lo
-    flat = span < 1e-8
-    one = torch.ones_like(lo)
-    # tensor / tensor: a division by a Python scalar may be lowered to a
-    # multiplication by its reciprocal on some devices, which rounds differently
-    s = torch.where(flat, torch.where(lo == 0, one, lo.abs()), span / torch.full_like(span, 15.0)).clamp(min=1e-8)
-    z_live = torch.round(-lo / s).clamp(0, 15)
-    z = torch.where(flat, (lo < 0).to(torch.float32), z_live)
-    q_live = torch.round((wg - (-(z * s))) / s).clamp(0, 15)
-    q = torch.where(flat, (lo > 0).to(torch.float32).expand_as(wg), q_live).to(torch.uint8)
-    packed = (q[..., :16] | (q[..., 16:] << 4)).reshape(N, K // 2)
-    zb = z.to(torch.uint8).reshape(N, G)
-    if G % 2:
-        zb = torch.nn.functional.pad(zb, (0, 1))
-    packed_zeros = zb[:, 0::2] | (zb[:, 1::2] << 4)
-    return packed.contiguous(), s.reshape(N, G).to(torch.float16).contiguous(), packed_zeros.contiguous()
+    dev = w.device
+    packed = torch.empty(N, K // 2, dtype=torch.uint8, device=dev)
+    scales = torch.empty(N, G, dtype=torch.float16, device=dev)
+    zeros = torch.empty(N, G, dtype=torch.uint8, device=dev)
+    pz = torch.empty(N, (G + 1) // 2, dtype=torch.uint8, device=dev)
+    idx = None
+    if outlier_idx is not None and outlier_idx.numel():
+        _cuda("outlier_idx", outlier_idx)
+        idx = outlier_idx.reshape(-1)
+        if idx.dtype not in (torch.int32, torch.int64):
+            idx = idx.to(torch.int64)
+        idx = idx.contiguous()
+    if N == 0:
+        return packed, scales, zeros, pz
+    with torch.cuda.device(dev):
+        st = L.lib().spectra_quantize_group32(
+            w.data_ptr(), _DT[w.dtype], w.stride(0),
+            idx.data_ptr() if idx is not None else None, _DT[idx.dtype] if idx is not None else 0,
+            idx.numel() if idx is not None else 0,
+            packed.data_ptr(), packed.stride(0), scales.data_ptr(), scales.stride(0),
+            zeros.data_ptr(), zeros.stride(0), pz.data_ptr(), pz.stride(0),
+            N, K, L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD,
+            torch.cuda.current_stream(dev).cuda_stream)
+    L.check("spectra_quantize_group32", st)
+    return packed, scales, zeros, pz
 
 
 def unpack_zeros(packed_zeros: torch.Tensor, K: int) -> torch.Tensor:
-    """Two zero points per byte -> one u8 per group (spectra/engine.py:1007-1012)."""
-    lo = packed_zeros & 0x0F
-    hi = (packed_zeros >> 4) & 0x0F
-    z = torch.stack([lo, hi], dim=-1).reshape(packed_zeros.shape[0], -1)
-    return z[:, : K // GROUP].contiguous()
+    """Two zero points per byte -> one u8 per group (spectra/engine.py:1007-1012), on the GPU."""
+    _cuda("packed_zeros", packed_zeros)
+    if packed_zeros.dtype != torch.uint8 or packed_zeros.dim() != 2:
+        raise TypeError("packed_zeros must be a 2-D uint8 tensor")
+    pz = packed_zeros if packed_zeros.stride(1) == 1 else packed_zeros.contiguous()
+    N = pz.shape[0]
+    G = K // GROUP
+    if pz.shape[1] * 2 < G:
+        raise ValueError(f"packed_zeros has {pz.shape[1]} bytes per row; K={K} needs {(G + 1) // 2}")
+    z = torch.empty(N, G, dtype=torch.uint8, device=pz.device)
+    if N == 0 or G == 0:
+        return z
+    with torch.cuda.device(pz.device):
+        st = L.lib().spectra_unpack_zeros(pz.data_ptr(), pz.stride(0), z.data_ptr(), z.stride(0), N, G,
+                                          torch.cuda.current_stream(pz.device).cuda_stream)
+    L.check("spectra_unpack_zeros", st)
+    return z
 
 
 def select_outliers(w: torch.Tensor, norm_vector: Optional[torch.Tensor] = None,
@@ -105,10 +141,9 @@ def select_outliers(w: torch.Tensor, norm_vector: Optional[torch.Tensor] = None,
 
 
 def compress_linear(w: torch.Tensor, norm_vector: Optional[torch.Tensor] = None) -> CompressedLinear:
-    """Everything ``SpectraFusedLinear.set_weights`` receives for weight ``w``."""
+    """Everything ``SpectraFusedLinear.set_weights`` receives for weight ``w`` (CUDA)."""
+    _cuda("w", w)
     idx, ratio, kurt = select_outliers(w, norm_vector)
     ow = w[:, idx].contiguous()
-    wz = w.clone()
-    wz[:, idx] = 0
-    packed, scales, pz = quantize_group32(wz)
-    return CompressedLinear(packed, scales, unpack_zeros(pz, w.shape[1]), pz, idx, ow, ratio, kurt)
+    packed, scales, zeros, pz = quantize_group32(w, idx)
+    return CompressedLinear(packed, scales, zeros, pz, idx, ow, ratio, kurt)

@@ -3,10 +3,12 @@
 // CUDA call, so an invalid call returns a status code and launches nothing.
 #include <cuda.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdlib>
 
 #include "common.cuh"
+#include "format.h"
 #include "gemm.h"
 #include "gemv.h"
 
@@ -245,6 +247,139 @@ int spectra_device_timeouts(int64_t* count, int reset) {
 }
 
 int spectra_selftest_wait_timeout(void* stream) { return launch_selftest_wait(static_cast<cudaStream_t>(stream)); }
+
+int spectra_quantize_group32(
+    const void* w, int w_dtype, int64_t w_row_stride,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    uint8_t* packed, int64_t p_row_stride,
+    uint16_t* scales, int64_t s_row_stride,
+    uint8_t* zeros, int64_t z_row_stride,
+    uint8_t* packed_zeros, int64_t pz_row_stride,
+    int64_t N, int64_t K, int layout, void* stream) {
+  if (!w || !packed || !scales) return SPECTRA_ERR_NULL_POINTER;
+  if (N <= 0 || K <= 0 || K % kGroup != 0 || !fits_i32(N) || !fits_i32(K)) return SPECTRA_ERR_SHAPE;
+  if (!is_float_dt(w_dtype)) return SPECTRA_ERR_DTYPE;
+  if (layout != SPECTRA_LAYOUT_MARLIN && layout != SPECTRA_LAYOUT_EVEN_ODD) return SPECTRA_ERR_UNSUPPORTED;
+  if (n_out < 0 || !fits_i32(n_out)) return SPECTRA_ERR_SHAPE;
+  if (n_out > 0 && !outlier_idx) return SPECTRA_ERR_NULL_POINTER;
+  if (n_out > 0 && !is_index_dt(idx_dtype)) return SPECTRA_ERR_DTYPE;
+  const int64_t G = K / kGroup;
+  if (w_row_stride < K || p_row_stride < K / 2 || s_row_stride < G || (zeros && z_row_stride < G) ||
+      (packed_zeros && pz_row_stride < (G + 1) / 2))
+    return SPECTRA_ERR_STRIDE;
+  if (!aligned(w, dt_size(w_dtype)) || !aligned(scales, 2) || (n_out > 0 && !aligned(outlier_idx, dt_size(idx_dtype))))
+    return SPECTRA_ERR_ALIGNMENT;
+  QuantArgs a;
+  a.w = w; a.w_dtype = w_dtype; a.w_rs = w_row_stride;
+  a.idx = n_out > 0 ? outlier_idx : nullptr; a.idx_dtype = idx_dtype; a.n_out = int(n_out);
+  a.packed = packed; a.p_rs = p_row_stride; a.packed_vec = aligned(packed, 16) && p_row_stride % 16 == 0;
+  a.scales = scales; a.s_rs = s_row_stride;
+  a.zeros = zeros; a.z_rs = z_row_stride;
+  a.packed_zeros = packed_zeros; a.pz_rs = pz_row_stride;
+  a.N = int(N); a.K = int(K); a.layout = layout;
+  return launch_quantize_group32(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_unpack_zeros(const uint8_t* packed_zeros, int64_t pz_row_stride, uint8_t* zeros, int64_t z_row_stride,
+                         int64_t N, int64_t G, void* stream) {
+  if (!packed_zeros || !zeros) return SPECTRA_ERR_NULL_POINTER;
+  if (N <= 0 || G <= 0 || !fits_i32(G)) return SPECTRA_ERR_SHAPE;
+  if (pz_row_stride < (G + 1) / 2 || z_row_stride < G) return SPECTRA_ERR_STRIDE;
+  UnpackZerosArgs a;
+  a.packed_zeros = packed_zeros; a.pz_rs = pz_row_stride;
+  a.zeros = zeros; a.z_rs = z_row_stride;
+  a.N = N; a.G = int(G);
+  return launch_unpack_zeros(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_kv_quantize(const void* t, int t_dtype, int64_t rows, int64_t D, uint8_t* packed, uint16_t* scales,
+                        uint8_t* zeros, void* stream) {
+  if (!t || !packed || !scales || !zeros) return SPECTRA_ERR_NULL_POINTER;
+  if (rows < 0 || D <= 0 || !fits_i32(D)) return SPECTRA_ERR_SHAPE;
+  if (t_dtype != SPECTRA_DT_BF16 && t_dtype != SPECTRA_DT_F16) return SPECTRA_ERR_DTYPE;
+  if (!aligned(t, 2) || !aligned(packed, 16) || !aligned(scales, 2)) return SPECTRA_ERR_ALIGNMENT;
+  if (rows == 0) return SPECTRA_OK;
+  KvQuantArgs a;
+  a.t = t; a.t_dtype = t_dtype; a.rows = rows; a.D = int(D);
+  a.packed = packed; a.scales = scales; a.zeros = zeros;
+  return launch_kv_quantize(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_kv_dequantize(const uint8_t* packed, const uint16_t* scales, const uint8_t* zeros, void* out,
+                          int out_dtype, int64_t rows, int64_t D, void* stream) {
+  if (!packed || !scales || !zeros || !out) return SPECTRA_ERR_NULL_POINTER;
+  if (rows < 0 || D <= 0 || !fits_i32(D)) return SPECTRA_ERR_SHAPE;
+  if (!is_float_dt(out_dtype)) return SPECTRA_ERR_DTYPE;
+  if (!aligned(packed, 16) || !aligned(scales, 2) || !aligned(out, dt_size(out_dtype))) return SPECTRA_ERR_ALIGNMENT;
+  if (rows == 0) return SPECTRA_OK;
+  KvDequantArgs a;
+  a.packed = packed; a.scales = scales; a.zeros = zeros;
+  a.out = out; a.out_dtype = out_dtype; a.rows = rows; a.D = int(D);
+  return launch_kv_dequantize(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_w4a16_embedding(
+    const void* ids, int ids_dtype, int64_t T,
+    const uint8_t* packed, int64_t w_row_stride,
+    const uint16_t* scales, int64_t s_row_stride,
+    const uint8_t* zeros, int64_t z_row_stride, int zeros_packed,
+    const void* outlier_idx, int idx_dtype, int64_t n_out,
+    const void* outlier_w, int ow_dtype, int64_t ow_row_stride,
+    void* out, int out_dtype, int64_t out_row_stride,
+    int64_t V, int64_t K, int layout, void* stream) {
+  if (!ids || !packed || !scales || !zeros || !out) return SPECTRA_ERR_NULL_POINTER;
+  if (T < 0 || V <= 0 || K <= 0 || K % kGroup != 0 || !fits_i32(K)) return SPECTRA_ERR_SHAPE;
+  if (!is_index_dt(ids_dtype) || !is_float_dt(out_dtype)) return SPECTRA_ERR_DTYPE;
+  if (layout != SPECTRA_LAYOUT_MARLIN && layout != SPECTRA_LAYOUT_EVEN_ODD) return SPECTRA_ERR_UNSUPPORTED;
+  if (n_out < 0 || !fits_i32(n_out)) return SPECTRA_ERR_SHAPE;
+  if (n_out > 0 && (!outlier_idx || !outlier_w)) return SPECTRA_ERR_NULL_POINTER;
+  if (n_out > 0 && (!is_index_dt(idx_dtype) || !is_float_dt(ow_dtype))) return SPECTRA_ERR_DTYPE;
+  const int64_t G = K / kGroup;
+  if (w_row_stride < K / 2 || s_row_stride < G || z_row_stride < (zeros_packed ? (G + 1) / 2 : G) ||
+      out_row_stride < K || (n_out > 0 && ow_row_stride < n_out))
+    return SPECTRA_ERR_STRIDE;
+  if (!aligned(ids, dt_size(ids_dtype)) || !aligned(scales, 2) || !aligned(out, dt_size(out_dtype)) ||
+      (n_out > 0 && (!aligned(outlier_idx, dt_size(idx_dtype)) || !aligned(outlier_w, dt_size(ow_dtype)))))
+    return SPECTRA_ERR_ALIGNMENT;
+  EmbedArgs a;
+  a.ids = ids; a.ids_dtype = ids_dtype; a.T = T;
+  a.packed = packed; a.w_rs = w_row_stride;
+  a.scales = scales; a.s_rs = s_row_stride;
+  a.zeros = zeros; a.z_rs = z_row_stride; a.zeros_packed = zeros_packed ? 1 : 0;
+  a.idx = n_out > 0 ? outlier_idx : nullptr; a.idx_dtype = idx_dtype; a.n_out = int(n_out);
+  a.ow = n_out > 0 ? outlier_w : nullptr; a.ow_dtype = ow_dtype; a.ow_rs = ow_row_stride;
+  a.out = out; a.out_dtype = out_dtype; a.out_rs = out_row_stride;
+  a.V = V; a.K = int(K); a.layout = layout;
+  return launch_embedding(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_argmax(const void* x, int x_dtype, int64_t x_row_stride, int64_t M, int64_t N, int64_t idx_offset,
+                   int64_t* idx, float* val, void* stream) {
+  if (!x || !idx) return SPECTRA_ERR_NULL_POINTER;
+  if (M < 0 || N <= 0) return SPECTRA_ERR_SHAPE;
+  if (!is_float_dt(x_dtype)) return SPECTRA_ERR_DTYPE;
+  if (M > 1 && x_row_stride < N) return SPECTRA_ERR_STRIDE;
+  if (!aligned(x, dt_size(x_dtype)) || !aligned(idx, 8) || (val && !aligned(val, 4))) return SPECTRA_ERR_ALIGNMENT;
+  ArgmaxArgs a;
+  a.x = x; a.x_dtype = x_dtype; a.x_rs = x_row_stride;
+  a.idx = idx; a.val = val; a.M = M; a.N = N; a.idx_offset = idx_offset;
+  return launch_argmax(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_fwht(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype, int64_t y_row_stride,
+                 int64_t M, int64_t n, int normalize, void* stream) {
+  if (!x || !y) return SPECTRA_ERR_NULL_POINTER;
+  if (M < 0 || n <= 0 || n > 32768 || (n & (n - 1)) != 0) return SPECTRA_ERR_SHAPE;
+  if (!is_float_dt(x_dtype) || !is_float_dt(y_dtype)) return SPECTRA_ERR_DTYPE;
+  if (M > 1 && (x_row_stride < n || y_row_stride < n)) return SPECTRA_ERR_STRIDE;
+  if (!aligned(x, dt_size(x_dtype)) || !aligned(y, dt_size(y_dtype))) return SPECTRA_ERR_ALIGNMENT;
+  FwhtArgs a;
+  a.x = x; a.x_dtype = x_dtype; a.x_rs = x_row_stride;
+  a.y = y; a.y_dtype = y_dtype; a.y_rs = y_row_stride;
+  a.M = M; a.n = int(n); a.normalize = normalize ? 1 : 0;
+  a.inv_norm = float(std::sqrt(double(n)));  // the divisor, as the reference's res / math.sqrt(d)
+  return launch_fwht(a, static_cast<cudaStream_t>(stream));
+}
 
 size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;

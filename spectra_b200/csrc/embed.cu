@@ -1,0 +1,146 @@
+// Token-embedding gather-dequantise and greedy argmax for sm_100a.
+//
+// Embedding: replaces SpectraFusedEmbedding.forward (spectra/engine.py:167-212).
+// For every token id, the packed row of the quantised vocabulary matrix is
+// dequantised -- ((q - z) * s) in fp32, exact, then rounded once to the output
+// dtype -- and the outlier columns are overwritten with the exact outlier
+// weights rounded to the output dtype (:207-210).  Zero points may be given
+// unpacked (one byte per group) or packed two per byte (:176-183).  A token id
+// outside [0, V) writes a row of zeros instead of reading out of bounds (the
+// reference's torch indexing would raise).  One CTA per token: thread i
+// dequantises group i (16 bytes -> 32 outputs), then the outlier columns.
+//
+// Argmax: the greedy next-token choice over logits [M, N] (the engine's
+// sample_token at temperature 0, spectra/engine.py:1690-1713, is
+// torch.argmax): first index of the maximum, a NaN counts as the maximum (as
+// in torch).  One CTA per row; `idx_offset` turns a shard's local index into
+// the layer's row index, so the N-sharded lm_head reduces (value, index)
+// pairs across ranks instead of gathering every logit.
+#include "common.cuh"
+#include "format.h"
+#include "gemv_mma.cuh"
+
+namespace spectra {
+
+namespace {
+
+constexpr int kEmbedThreads = 256;
+constexpr int kArgmaxThreads = 1024;
+
+__global__ void __launch_bounds__(kEmbedThreads) embedding_kernel(EmbedArgs a) {
+  const int64_t t = blockIdx.x;
+  const int64_t id = load_index(a.ids, t, a.ids_dtype);
+  const bool valid = id >= 0 && id < a.V;
+  const int G = a.K / kGroup;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    float v[kGroup];
+    if (valid) {
+      const uint4 w = load_group16<1>(a.packed + id * a.w_rs + int64_t(g) * kGroupBytes);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+      const float s = __half2float(__ushort_as_half(a.scales[id * a.s_rs + g]));
+      uint32_t zb;
+      if (a.zeros_packed) {
+        const uint8_t b = a.zeros[id * a.z_rs + (g >> 1)];
+        zb = (g & 1) ? (b >> 4) & 0xFu : b & 0xFu;
+      } else {
+        zb = a.zeros[id * a.z_rs + g];
+      }
+      const float z = float(zb);
+#pragma unroll
+      for (int byte = 0; byte < 16; ++byte) {
+        const uint32_t bv = (wv[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
+        v[code_k(byte, 0, a.layout)] = __fmul_rn(float(bv & 0xFu) - z, s);
+        v[code_k(byte, 1, a.layout)] = __fmul_rn(float(bv >> 4) - z, s);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kGroup; ++i) v[i] = 0.f;
+    }
+    const int64_t base = t * a.out_rs + int64_t(g) * kGroup;
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) store_from_float(a.out, base + i, a.out_dtype, v[i]);
+  }
+  if (a.n_out > 0 && valid) {
+    __syncthreads();  // the outlier columns overwrite what the loop above stored
+    for (int j = threadIdx.x; j < a.n_out; j += blockDim.x) {
+      const int64_t k = load_index(a.idx, j, a.idx_dtype);
+      if (k < 0 || k >= a.K) continue;
+      const float w = load_as_float(a.ow, id * a.ow_rs + j, a.ow_dtype);
+      store_from_float(a.out, t * a.out_rs + k, a.out_dtype, w);
+    }
+  }
+}
+
+// (value, index) order of torch.argmax: larger value first; NaN above every
+// number; on ties (and between NaNs) the smaller index.
+__device__ __forceinline__ bool better(float v, int64_t i, float bv, int64_t bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn || bn) return vn && (!bn || i < bi);
+  return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(ArgmaxArgs a) {
+  const int64_t m = blockIdx.x;
+  float bv = -INFINITY;
+  int64_t bi = INT64_MAX;
+  for (int64_t n = threadIdx.x; n < a.N; n += blockDim.x) {
+    const float v = load_as_float_cg(a.x, m * a.x_rs + n, a.x_dtype);
+    if (better(v, n, bv, bi)) {
+      bv = v;
+      bi = n;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int64_t si[kArgmaxThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x / 32;
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      a.idx[m] = (bi == INT64_MAX ? 0 : bi) + a.idx_offset;
+      if (a.val) a.val[m] = bv;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_embedding(const EmbedArgs& a, cudaStream_t st) {
+  if (a.T == 0) return SPECTRA_OK;
+  if (a.T > int64_t(INT32_MAX)) return SPECTRA_ERR_SHAPE;
+  embedding_kernel<<<unsigned(a.T), kEmbedThreads, 0, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_argmax(const ArgmaxArgs& a, cudaStream_t st) {
+  if (a.M == 0) return SPECTRA_OK;
+  if (a.M > int64_t(INT32_MAX)) return SPECTRA_ERR_SHAPE;
+  argmax_kernel<<<unsigned(a.M), kArgmaxThreads, 0, st>>>(a);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace spectra

@@ -106,11 +106,19 @@ def fused_w4a16_gemv_hdsq(
     outlier_w: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
     marlin_layout: bool = False,
+    hadamard: bool = False,
 ) -> torch.Tensor:
-    """M=1 W4A16 GEMV with fused outlier and bias adds (spectra/kernels.py:132-184)."""
+    """M=1 W4A16 GEMV with fused outlier and bias adds (spectra/kernels.py:132-184).
+
+    ``hadamard`` (keyword, off by default, not in the reference signature):
+    rotate x by the normalised Walsh-Hadamard transform first (the rotation
+    prologue for weights quantised in the rotated basis; K a power of two).
+    """
     orig_dim = x.ndim
     if orig_dim == 1:
         x = x.unsqueeze(0)
+    if hadamard:
+        x = fwht(x, normalize=True)
     B, K = x.shape
     N = packed_w.shape[0]
     dev = x.device
@@ -257,3 +265,103 @@ def dequantize(packed_w: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor
             N, K, L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD, _stream(dev))
     L.check("spectra_w4a16_dequant", st)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Operators around the linear path: rotation prologue, embedding gather,
+# greedy argmax (csrc/fwht.cu, csrc/embed.cu)
+# ---------------------------------------------------------------------------
+
+def fwht(x: torch.Tensor, normalize: bool = True, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Walsh-Hadamard transform of the rows of ``x`` [..., n] on the GPU (the
+    reference's fast_walsh_hadamard_transform, spectra/compressor.py:29-42):
+    butterflies in fp32, divided by sqrt(n) if ``normalize``, rounded once to
+    ``out_dtype`` (default: x's dtype).  n must be a power of two <= 32768."""
+    _require_cuda("x", x, x.device)
+    n = x.shape[-1]
+    x2 = x.reshape(-1, n)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    y = torch.empty(x2.shape, dtype=out_dtype or x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        st = L.lib().spectra_fwht(x2.data_ptr(), _dt(x2), x2.stride(0), y.data_ptr(), _dt(y), y.stride(0),
+                                  x2.shape[0], n, int(normalize), _stream(x.device))
+    L.check("spectra_fwht", st)
+    return y.reshape(x.shape)
+
+
+def embedding(input_ids: torch.Tensor, packed_w: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+              outlier_idx: Optional[torch.Tensor] = None, outlier_w: Optional[torch.Tensor] = None,
+              marlin_layout: bool = False, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Gather-dequantise the rows ``input_ids`` of a quantised [V, K] matrix
+    (SpectraFusedEmbedding.forward, spectra/engine.py:167-212): exact
+    ``(q - z) * s`` rounded once to ``out_dtype``, outlier columns restored from
+    ``outlier_w``.  ``zeros`` may be unpacked [V, K/32] or packed two per byte."""
+    dev = packed_w.device
+    for name, t in (("input_ids", input_ids), ("packed_w", packed_w), ("scales", scales), ("zeros", zeros),
+                    ("outlier_idx", outlier_idx), ("outlier_w", outlier_w)):
+        _require_cuda(name, t, dev)
+    packed, scales, zeros = _weights(packed_w, scales, zeros)
+    V, K = packed.shape[0], packed.shape[1] * 2
+    G = K // 32
+    zeros_packed = zeros.shape[1] < G
+    if scales.stride(1) != 1:
+        scales = scales.contiguous()
+    if zeros.stride(1) != 1:
+        zeros = zeros.contiguous()
+    ids = input_ids.reshape(-1)
+    if ids.dtype not in (torch.int32, torch.int64):
+        ids = ids.to(torch.int64)
+    ids = ids.contiguous()
+    idx, ow, n_out = _outliers(outlier_idx, outlier_w, V)
+    if ow is not None and ow.stride(1) != 1:
+        ow = ow.contiguous()
+    out = torch.empty(ids.numel(), K, dtype=out_dtype, device=dev)
+    if ids.numel():
+        with torch.cuda.device(dev):
+            st = L.lib().spectra_w4a16_embedding(
+                ids.data_ptr(), _dt(ids), ids.numel(),
+                packed.data_ptr(), packed.stride(0), scales.data_ptr(), scales.stride(0),
+                zeros.data_ptr(), zeros.stride(0), int(zeros_packed),
+                idx.data_ptr() if idx is not None else None, _dt(idx) if idx is not None else 0, n_out,
+                ow.data_ptr() if ow is not None else None, _dt(ow) if ow is not None else 0,
+                ow.stride(0) if ow is not None else 0,
+                out.data_ptr(), _dt(out), out.stride(0), V, K,
+                L.LAYOUT_MARLIN if marlin_layout else L.LAYOUT_EVEN_ODD, _stream(dev))
+        L.check("spectra_w4a16_embedding", st)
+    return out.reshape(tuple(input_ids.shape) + (K,))
+
+
+def argmax(logits: torch.Tensor, idx_offset: int = 0, with_values: bool = False):
+    """Greedy choice over the last dimension of ``logits`` [..., N] (the
+    engine's temperature-0 sample_token, spectra/engine.py:1690-1713): int64
+    index of the first maximum (NaN counts as the maximum, as torch.argmax)
+    plus ``idx_offset``; with ``with_values`` also the maxima as fp32."""
+    _require_cuda("logits", logits, logits.device)
+    N = logits.shape[-1]
+    x2 = logits.reshape(-1, N)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    idx = torch.empty(M, dtype=torch.int64, device=logits.device)
+    val = torch.empty(M, dtype=torch.float32, device=logits.device) if with_values else None
+    with torch.cuda.device(logits.device):
+        st = L.lib().spectra_argmax(x2.data_ptr(), _dt(x2), x2.stride(0), M, N, int(idx_offset), idx.data_ptr(),
+                                    val.data_ptr() if val is not None else None, _stream(logits.device))
+    L.check("spectra_argmax", st)
+    shape = tuple(logits.shape[:-1])
+    if with_values:
+        return idx.reshape(shape), val.reshape(shape)
+    return idx.reshape(shape)
+
+
+def lm_head_greedy(x: torch.Tensor, packed_w: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
+                   bias: Optional[torch.Tensor] = None, outlier_idx: Optional[torch.Tensor] = None,
+                   outlier_w: Optional[torch.Tensor] = None, marlin_layout: bool = False,
+                   out: Optional[torch.Tensor] = None):
+    """Greedy decode head at M=1: the lm_head GEMV (logits in x's dtype, as the
+    engine's tied head computes them, spectra/engine.py:1124-1168) followed on
+    the same stream by the argmax kernel.  Returns (next_token int64 [1], logits)."""
+    logits = fused_w4a16_gemv_hdsq(x, packed_w, scales, zeros, bias=bias, outlier_idx=outlier_idx,
+                                   outlier_w=outlier_w, out=out, marlin_layout=marlin_layout)
+    return argmax(logits.reshape(1, -1)), logits

@@ -22,6 +22,10 @@ numpy oracle in ``oracle/w4a16.py`` against the reference:
                        compressor output and the reference GEMV output.
 * fwht_cases.npz    -- the reference's (dead-code) Walsh-Hadamard transform,
                        oracle for the optional rotation prologue.
+* kv_cases.npz      -- the INT4 KV-cache quantiser / dequantiser
+                       (SpectraGroup32QuantizedLayer, spectra/engine.py:625-671) run on CPU.
+* embedding_cases.npz -- the quantised embedding gather (SpectraFusedEmbedding.forward,
+                       spectra/engine.py:167-212).
 * chunked.json      -- sha256 of the compressor outputs on an N>4096 matrix
                        (the row-chunked code path, spectra/compressor.py:143-156,168-174).
 
@@ -289,8 +293,65 @@ def config1():
     (HERE / "config1.json").write_text(json.dumps(rec))
 
 
+def kv_cases():
+    """The reference's INT4 KV-cache quantiser / dequantiser
+    (SpectraGroup32QuantizedLayer._quantize / _dequantize, spectra/engine.py:625-671),
+    run here on the CPU, on bf16 and fp16 key-like tensors (D = 64, 128, and 80,
+    which needs zero padding), including constant and all-zero rows."""
+    from spectra.engine import SpectraGroup32QuantizedLayer as QL
+
+    class _Holder:  # the two methods only read group_size
+        group_size = 32
+
+    h = _Holder()
+    out = {}
+    for name, shape, dt in (("bf16_d64", (2, 4, 9, 64), torch.bfloat16), ("bf16_d128", (1, 2, 5, 128), torch.bfloat16),
+                            ("f16_d64", (1, 3, 7, 64), torch.float16), ("bf16_d80", (2, 2, 3, 80), torch.bfloat16)):
+        torch.manual_seed(700 + shape[-1] + len(name))
+        t = (torch.randn(*shape) * 1.5).to(dt)
+        flat = t.reshape(-1, shape[-1])
+        flat[0] = 0.0
+        flat[1] = 0.75
+        flat[2, :32] = -2.0
+        packed, scales, zeros, orig_shape, pad = QL._quantize(h, t)
+        deq = QL._dequantize(h, (packed, scales, zeros, orig_shape, pad))
+        out[f"{name}/t"] = bits(t)
+        out[f"{name}/dtype"] = np.array("bf16" if dt == torch.bfloat16 else "f16")
+        out[f"{name}/packed"] = packed.numpy()
+        out[f"{name}/scales"] = bits(scales)
+        out[f"{name}/zeros"] = zeros.numpy()
+        out[f"{name}/pad"] = np.array(pad)
+        out[f"{name}/deq"] = bits(deq)
+    np.savez_compressed(HERE / "kv_cases.npz", **out)
+
+
+def embedding_cases():
+    """The reference's quantised embedding gather (SpectraFusedEmbedding.forward,
+    spectra/engine.py:167-212) on compressor output for a small vocabulary,
+    Marlin and even-odd orders, unpacked and packed zero points, bf16 and fp16
+    targets, repeated token ids."""
+    from spectra.engine import SpectraFusedEmbedding
+    comp = SpectraCompressor()
+    V, K = 300, 256
+    w = draw_weight(V, K, seed=41, dist="t3")
+    w_dense, idx, ow, ratio, kurt = comp._isolate_hdsq_outliers(w)
+    p, s, pz = SpectraCompressor._compute_group32_quant(w_dense)
+    zc = unpack_zeros_t(pz, K)
+    ids = torch.tensor([[0, 5, 5, 299], [17, 128, 3, 250]], dtype=torch.int64)
+    out = {"packed": p.numpy(), "scales": bits(s), "packed_zeros": pz.numpy(), "zeros": zc.numpy(),
+           "idx": idx.long().numpy(), "ow": bits(ow), "ids": ids.numpy()}
+    for tag, marlin, zeros, tdt in (("marlin_unpacked_bf16", True, zc, torch.bfloat16),
+                                    ("marlin_packed_f16", True, pz, torch.float16),
+                                    ("evenodd_unpacked_bf16", False, zc, torch.bfloat16)):
+        emb = SpectraFusedEmbedding(V, K, marlin_layout=marlin)
+        emb.set_weights(p, s, zeros, outlier_idx=idx.long(), outlier_weight=ow, marlin_layout=marlin)
+        emb.target_dtype = tdt
+        out[f"{tag}/y"] = bits(emb(ids))
+    np.savez_compressed(HERE / "embedding_cases.npz", **out)
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["quant", "outlier", "chunked", "kernel", "config1", "fwht"]
+    which = sys.argv[1:] or ["quant", "outlier", "chunked", "kernel", "config1", "fwht", "kv", "embedding"]
     if "quant" in which:
         quant_cases()
     if "outlier" in which:
@@ -303,4 +364,8 @@ if __name__ == "__main__":
         config1()
     if "fwht" in which:
         fwht_cases()
+    if "kv" in which:
+        kv_cases()
+    if "embedding" in which:
+        embedding_cases()
     print("golden fixtures written to", HERE)
