@@ -465,12 +465,13 @@ def run_gpu(args, world, rank, local):
     def steps(n):
         (timed_graph if n == args.steps else warm_graph).replay()
 
-    steps(max(args.warmup, 1))
-    torch.cuda.synchronize(dev)
-
     clk = ClockSampler(local)
     clk.start()
-    time.sleep(0.3)
+    time.sleep(0.3)  # the sampler's first readings
+    # warm-up steps right before the timed region: no idle gap in between for
+    # the clocks to drop into
+    steps(max(args.warmup, 1))
+    torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     w0 = time.time()

@@ -185,6 +185,8 @@ def batched_w4a16_gemm(
     outlier_idx: Optional[torch.Tensor] = None,
     outlier_w: Optional[torch.Tensor] = None,
     marlin_layout: bool = False,
+    *,
+    out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """M >= 2 W4A16 GEMM on the tcgen05 tensor cores (spectra/kernels.py:333-389).
 
@@ -192,6 +194,10 @@ def batched_w4a16_gemm(
     to the compute dtype (bf16 if ``a`` is bf16, else fp16) exactly as the
     reference does; fp32 ``a`` is rounded to fp16 before the call, the same
     rounding the reference applies when it loads it.  No bias is added.
+
+    ``out`` (keyword, not in the reference signature): a [M, N] tensor of the
+    compute dtype with unit column stride to write into (for example a view
+    into a larger buffer); it is returned, reshaped like ``a``.
     """
     orig_shape = a.shape
     K = a.shape[-1]
@@ -205,7 +211,13 @@ def batched_w4a16_gemm(
     packed, scales, zeros = _weights(packed_b, scales, zeros)
     idx, ow, n_out = _outliers(outlier_idx, outlier_w, N)
     compute = torch.bfloat16 if a.dtype == torch.bfloat16 else torch.float16
-    c = torch.empty((M, N), device=dev, dtype=compute)
+    if out is not None:
+        _require_cuda("out", out, dev)
+        if out.dtype != compute or tuple(out.shape) != (M, N) or (N > 1 and out.stride(1) != 1):
+            raise ValueError(f"out must be a [{M}, {N}] {compute} tensor with unit column stride")
+        c = out
+    else:
+        c = torch.empty((M, N), device=dev, dtype=compute)
     if M == 0 or N == 0:
         return c.reshape(orig_shape[:-1] + (N,)).to(a.dtype)
     a2 = a.reshape(M, K)
@@ -242,6 +254,8 @@ def batched_w4a16_gemm(
             M, N, K, layout,
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, stream)
     L.check("spectra_w4a16_gemm", st)
+    if out is not None:
+        return c
     return c.reshape(orig_shape[:-1] + (N,)).to(a.dtype)
 
 

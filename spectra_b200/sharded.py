@@ -6,13 +6,20 @@ scales, zero points, outlier weights and bias; ``outlier_idx`` (columns of x)
 and the activations x are replicated.  Each rank computes its [M, Ns] slice
 with the same kernels as the unsharded layer (the M=1 GEMV with bias fused,
 else the tensor-core GEMM plus bias, exactly as ``SpectraFusedLinear.forward``
-routes them, spectra/engine.py:90-124), then one all-gather over the process
-group assembles [M, N].  This is the only collective: the slices are
-independent.
+routes them, spectra/engine.py:90-124), writing straight into a persistent
+[M, Ns] buffer of this rank (rows past N stay zero: a ragged last shard costs
+no extra kernel), then one all-gather over the process group assembles
+[M, N].  This is the only collective: the slices are independent.
 
 The gathered buffer is laid out [g, M, Ns]; for M = 1 it already is the output
-row (no copy), for M > 1 one transpose copy makes it [M, N].  Rows of the last
-shard past N are zero and dropped.
+row (no copy), for M > 1 one transpose copy makes it [M, N].
+
+Greedy decode does not need the whole row of logits on every rank:
+``greedy(x)`` computes this rank's slice, its first maximum with the argmax
+kernel (the layer's row index), and all-gathers one (value, index) pair per
+rank -- 16 bytes instead of N logits -- before picking the first maximum in
+rank order, which is row order (the engine's temperature-0 sample_token is a
+torch.argmax, spectra/engine.py:1690-1713).
 
 The reference has no multi-GPU path (no collective call sites); this module is
 the sharding the hot path's large layers (lm_head, 8192 x 28672) need on an
@@ -21,7 +28,7 @@ gather latency is counted, so callers shard only large layers.
 """
 from __future__ import annotations
 
-from typing import Callable, Optional
+from typing import Callable, Dict, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -37,15 +44,24 @@ def shard_bounds(N: int, world: int, rank: int):
     return ns, lo, hi
 
 
-def _kernel_local(x2d, packed, scales, zeros, outlier_idx, outlier_w, bias, marlin_layout):
-    """This rank's slice with the production kernels (spectra/engine.py:97-124 routing)."""
+def _kernel_local(x2d, packed, scales, zeros, outlier_idx, outlier_w, bias, marlin_layout, out):
+    """This rank's slice with the production kernels (spectra/engine.py:97-124
+    routing), written into ``out`` ([M, rows] view of the rank's buffer)."""
     from . import kernels as SK
     if x2d.shape[0] == 1:
-        return SK.fused_w4a16_gemv_hdsq(x2d, packed, scales, zeros, bias=bias, outlier_idx=outlier_idx,
-                                        outlier_w=outlier_w, marlin_layout=marlin_layout)
-    y = SK.batched_w4a16_gemm(x2d, packed, scales, zeros, outlier_idx=outlier_idx, outlier_w=outlier_w,
-                              marlin_layout=marlin_layout)
-    return y + bias if bias is not None else y
+        SK.fused_w4a16_gemv_hdsq(x2d, packed, scales, zeros, bias=bias, outlier_idx=outlier_idx,
+                                 outlier_w=outlier_w, out=out, marlin_layout=marlin_layout)
+        return
+    SK.batched_w4a16_gemm(x2d, packed, scales, zeros, outlier_idx=outlier_idx, outlier_w=outlier_w,
+                          marlin_layout=marlin_layout, out=out)
+    if bias is not None:
+        out += bias
+
+
+def _kernel_argmax(y: torch.Tensor, offset: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    from . import kernels as SK
+    idx, val = SK.argmax(y, idx_offset=offset, with_values=True)
+    return val, idx
 
 
 class ShardedW4A16Linear:
@@ -54,21 +70,24 @@ class ShardedW4A16Linear:
 
     ``packed``/``scales``/``zeros``/``outlier_w``/``bias`` are the FULL layer
     tensors (any device); the constructor keeps this rank's rows, moved to
-    ``device``.  ``local_fn`` computes one rank's slice; it defaults to the CUDA
-    kernels (tests on CPU pass a reference implementation instead).
+    ``device``.  ``local_fn(x2d, packed, scales, zeros, idx, ow, bias, marlin,
+    out)`` writes one rank's slice into ``out``; it defaults to the CUDA kernels
+    (tests on CPU pass a reference implementation instead), as does
+    ``argmax_fn(y, offset) -> (values, indices)``.
     """
 
     def __init__(self, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                  outlier_idx: Optional[torch.Tensor] = None, outlier_w: Optional[torch.Tensor] = None,
                  bias: Optional[torch.Tensor] = None, marlin_layout: bool = False,
                  group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None,
-                 local_fn: Optional[Callable] = None):
+                 local_fn: Optional[Callable] = None, argmax_fn: Optional[Callable] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.N = packed.shape[0]
         self.in_features = packed.shape[1] * 2
         self.ns, lo, hi = shard_bounds(self.N, self.world, self.rank)
+        self.row0 = lo
         self.rows = hi - lo
         dev = device if device is not None else packed.device
         self.device = dev
@@ -81,25 +100,34 @@ class ShardedW4A16Linear:
         self.bias = take(bias)
         self.marlin_layout = marlin_layout
         self.local_fn = local_fn or _kernel_local
+        self.argmax_fn = argmax_fn or _kernel_argmax
+        self._local_bufs: Dict[Tuple[int, torch.dtype], torch.Tensor] = {}
+
+    def _local_buffer(self, M: int, dtype: torch.dtype) -> torch.Tensor:
+        """Persistent [M, Ns] slice buffer: zero-filled once, so the rows past the
+        layer's end (ragged last shard) stay zero without a kernel per call."""
+        key = (M, dtype)
+        buf = self._local_bufs.get(key)
+        if buf is None:
+            buf = torch.zeros(M, self.ns, dtype=dtype, device=self.device)
+            self._local_bufs[key] = buf
+        return buf
 
     def local(self, x2d: torch.Tensor) -> torch.Tensor:
         """[M, Ns] slice of this rank (rows past the layer's end are zero)."""
         M = x2d.shape[0]
-        out = torch.zeros(M, self.ns, device=x2d.device, dtype=x2d.dtype) if self.rows < self.ns else None
-        if self.rows == 0:
-            return out
-        y = self.local_fn(x2d, self.packed, self.scales, self.zeros, self.outlier_idx, self.outlier_w,
-                          self.bias, self.marlin_layout)
-        if out is None:
-            return y.to(x2d.dtype).reshape(M, self.ns)
-        out[:, :self.rows] = y.reshape(M, self.rows)
-        return out
+        compute = torch.bfloat16 if x2d.dtype == torch.bfloat16 else torch.float16
+        buf = self._local_buffer(M, compute)
+        if self.rows > 0:
+            self.local_fn(x2d, self.packed, self.scales, self.zeros, self.outlier_idx, self.outlier_w,
+                          self.bias, self.marlin_layout, buf[:, :self.rows])
+        return buf
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         orig_shape = x.shape
         M = x.numel() // self.in_features
         x2d = x.reshape(M, self.in_features)
-        y_local = self.local(x2d).contiguous()
+        y_local = self.local(x2d)
         if self.world == 1:
             y = y_local[:, :self.N]
         else:
@@ -113,3 +141,27 @@ class ShardedW4A16Linear:
         return y.reshape(orig_shape[:-1] + (self.N,)).to(x.dtype)
 
     __call__ = forward
+
+    def greedy(self, x: torch.Tensor) -> torch.Tensor:
+        """Index of the first maximum of each output row [..., N] (int64), from
+        this rank's slice and one all-gather of (value, index) pairs."""
+        orig_shape = x.shape
+        M = x.numel() // self.in_features
+        x2d = x.reshape(M, self.in_features)
+        y_local = self.local(x2d)
+        if self.rows > 0:
+            val, idx = self.argmax_fn(y_local[:, :self.rows], self.row0)
+            pair = torch.stack([val.to(torch.float64), idx.to(torch.float64)], dim=1)  # [M, 2], exact
+        else:  # an empty shard never wins
+            pair = torch.tensor([[float("-inf"), float(2 ** 53)]], dtype=torch.float64,
+                                device=y_local.device).expand(M, 2).contiguous()
+        if self.world == 1:
+            return pair[:, 1].to(torch.int64).reshape(orig_shape[:-1])
+        gathered = torch.empty(self.world * M * 2, dtype=torch.float64, device=pair.device)
+        dist.all_gather_into_tensor(gathered, pair.reshape(-1), group=self.group)
+        g = gathered.view(self.world, M, 2)
+        # ranks hold increasing row ranges: the first maximum in rank order is the
+        # first maximum of the row (torch.argmax: the first NaN counts as maximum)
+        r = torch.argmax(g[:, :, 0], dim=0)
+        tok = g[:, :, 1].gather(0, r.view(1, M)).view(M)
+        return tok.to(torch.int64).reshape(orig_shape[:-1])

@@ -1,6 +1,7 @@
-"""Row-sharded linear (spectra_b200.sharded) on CPU: 2 gloo ranks, each computing
-its rows with the oracle, must assemble exactly the oracle's full-layer output
-(M = 1 and M > 1, ragged last shard, outliers, bias)."""
+"""Row-sharded linear (spectra_b200.sharded) on CPU: 2, 4 and 8 gloo ranks, each
+computing its rows with the oracle, must assemble exactly the oracle's
+full-layer output (M = 1 and M > 1, ragged and empty last shards, outliers,
+bias), and the sharded greedy head must pick the oracle's argmax."""
 import os
 import socket
 
@@ -19,9 +20,24 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _oracle_local(x2d, packed, scales, zeros, idx, ow, bias, marlin):
+def _oracle_local(x2d, packed, scales, zeros, idx, ow, bias, marlin, out=None):
     """One rank's slice by the oracle (the reference's routing: GEMV with bias at
-    M = 1, GEMM then + bias otherwise), rounded to x's dtype."""
+    M = 1, GEMM then + bias otherwise), rounded to x's dtype; written into
+    ``out`` when given (the module's local_fn contract)."""
+    y = _oracle_slice(x2d, packed, scales, zeros, idx, ow, bias, marlin)
+    if out is not None:
+        out.copy_(y)
+    return y
+
+
+def _oracle_argmax(y, offset):
+    from oracle import ops as P
+    yn = y.float().numpy()
+    i = P.argmax(yn)
+    return torch.from_numpy(yn[np.arange(len(i)), i]), torch.from_numpy(i + offset)
+
+
+def _oracle_slice(x2d, packed, scales, zeros, idx, ow, bias, marlin):
     from oracle import w4a16 as O
     xn = x2d.float().numpy().astype(np.float16)
     p, s, z = packed.numpy(), scales.numpy(), zeros.numpy()
@@ -56,16 +72,22 @@ def _worker(rank, world, port, cases, q):
         for N, K, n_out, M, seed in cases:
             p, s, z, idx, ow, bias = _layer(N, K, n_out, seed)
             lin = ShardedW4A16Linear(p, s, z, outlier_idx=idx, outlier_w=ow, bias=bias, marlin_layout=True,
-                                     device=torch.device("cpu"), local_fn=_oracle_local)
+                                     device=torch.device("cpu"), local_fn=_oracle_local, argmax_fn=_oracle_argmax)
             x = (torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 1))).to(torch.float16)
             y = lin(x)
-            res.append(y.numpy())
+            y2 = lin(x)  # the persistent slice buffer is reused
+            assert torch.equal(y, y2)
+            res.append((y.numpy(), lin.greedy(x).numpy()))
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
 
 
 CASES = [(256, 128, 4, 1, 1), (250, 128, 4, 1, 2), (250, 256, 0, 3, 3), (97, 64, 5, 2, 4)]
+# 4 and 8 ranks: ragged shards (1003 = 8 x 126 - 5), a shard count that leaves
+# the last ranks empty (9 rows over 8 ranks: 2,2,2,2,1,0,0,0), and a vocabulary-
+# shaped head (N = 1000 ~ 128256 / 128) at M = 1 and M > 1
+CASES_WIDE = [(1003, 128, 3, 1, 5), (9, 64, 2, 1, 6), (9, 64, 2, 3, 7), (1000, 256, 6, 1, 8), (1003, 128, 0, 4, 9)]
 
 
 def test_shard_bounds_cover_rows_once():
@@ -81,30 +103,45 @@ def test_shard_bounds_cover_rows_once():
         shard_bounds(10, 2, 2)
 
 
-def test_sharded_matches_full_layer_on_two_gloo_ranks():
+def _run_world(world, cases):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, CASES, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cases, q)) for r in range(world)]
     for pr in procs:
         pr.start()
-    got = dict(q.get(timeout=240) for _ in procs)
+    got = dict(q.get(timeout=300) for _ in procs)
     for pr in procs:
         pr.join(timeout=60)
         assert pr.exitcode == 0
-    for ci, (N, K, n_out, M, seed) in enumerate(CASES):
+    for ci, (N, K, n_out, M, seed) in enumerate(cases):
         p, s, z, idx, ow, bias = _layer(N, K, n_out, seed)
         x = (torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 1))).to(torch.float16)
         full = _oracle_local(x, p, s, z, idx if n_out else None, ow if n_out else None, bias, True).numpy()
-        for r in (0, 1):
-            assert got[r][ci].shape == (M, N)
-            np.testing.assert_array_equal(got[r][ci], full, err_msg=f"case {ci} rank {r}")
+        from oracle import ops as P
+        want_tok = P.argmax(full.astype(np.float32))
+        for r in range(world):
+            y, tok = got[r][ci]
+            assert y.shape == (M, N)
+            np.testing.assert_array_equal(y, full, err_msg=f"case {ci} rank {r}")
+            np.testing.assert_array_equal(tok, want_tok, err_msg=f"greedy, case {ci} rank {r}")
+
+
+def test_sharded_matches_full_layer_on_two_gloo_ranks():
+    _run_world(2, CASES)
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_sharded_ragged_and_empty_shards_on_many_gloo_ranks(world):
+    _run_world(world, CASES_WIDE)
 
 
 def test_single_process_is_unsharded():
     p, s, z, idx, ow, bias = _layer(64, 64, 3, 9)
     lin = ShardedW4A16Linear(p, s, z, outlier_idx=idx, outlier_w=ow, bias=bias, marlin_layout=True,
-                             device=torch.device("cpu"), local_fn=_oracle_local)
+                             device=torch.device("cpu"), local_fn=_oracle_local, argmax_fn=_oracle_argmax)
     assert lin.world == 1 and lin.rows == 64
     x = torch.randn(1, 64).to(torch.float16)
-    np.testing.assert_array_equal(lin(x).numpy(), _oracle_local(x, p, s, z, idx, ow, bias, True).numpy())
+    full = _oracle_local(x, p, s, z, idx, ow, bias, True).numpy()
+    np.testing.assert_array_equal(lin(x).numpy(), full)
+    assert int(lin.greedy(x)) == int(np.argmax(full.astype(np.float32)))

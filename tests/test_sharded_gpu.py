@@ -1,7 +1,8 @@
 """Row-sharded linear on GPUs: 2 NCCL ranks (one per GPU), each computing its
 rows with the CUDA kernels, must assemble the full layer's output -- the same
 on every rank and within the GEMV / GEMM parity bars of the oracle's result
-(M = 1 and M = 32, ragged last shard, outliers, bias).  Needs >= 2 GPUs."""
+(M = 1 and M = 32, ragged last shard, outliers, bias); the sharded greedy
+head picks the first maximum of that output.  Needs >= 2 GPUs."""
 import os
 import socket
 
@@ -50,8 +51,9 @@ def _worker(rank, world, port, q):
                                      device=torch.device("cuda", rank))
             x = torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 7)).to(torch.bfloat16)
             y = lin.forward(x.cuda(rank))
+            tok = lin.greedy(x.cuda(rank))
             torch.cuda.synchronize()
-            out.append(y.float().cpu().numpy())
+            out.append((y.float().cpu().numpy(), tok.cpu().numpy()))
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -72,8 +74,10 @@ def test_sharded_layer_on_two_gpus_matches_oracle():
         p.join(timeout=60)
         assert p.exitcode == 0
     for i, (N, K, n_out, M, seed) in enumerate(CASES):
-        y0, y1 = res[0][i], res[1][i]
+        (y0, t0), (y1, t1) = res[0][i], res[1][i]
         assert np.array_equal(y0, y1), f"ranks disagree on case {i}"
+        # the (value, index) reduction picks the first maximum of the gathered row
+        assert np.array_equal(t0, t1) and np.array_equal(t0, np.argmax(y0, axis=-1)), f"greedy, case {i}"
         f, bias = _layer(N, K, n_out, seed)
         x = torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 7)).to(torch.bfloat16)
         ow, owd = np_of(f["outlier_w_t"])
