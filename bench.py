@@ -27,10 +27,12 @@ M = 1 and 32, column-sharded over the job's GPUs with one NCCL all-gather, L2
 flushed before every call, slowest rank counted.
 
 ``--impl reference`` times the reference's CPU formula for the same layer
-(``oracle/cpu_path.py``) on the host cores instead.  Under torchrun (N>1) every
-rank runs the same single-GPU workload on its own layer copies (replicas:
-weak scaling, no collective on the data path) and the slowest rank's time
-counts; rank 0 prints one JSON line.
+(``oracle/cpu_path.py``) on the host cores instead.
+
+Under torchrun (N>1) the headline is BASELINE config 5 strong-scaled: the four
+Llama-3-70B linears at M=1, each column-sharded over the N ranks with one NCCL
+all-gather (``spectra_b200.sharded``); the slowest rank's device time counts
+and rank 0 prints one JSON line (with the all-gathers' share of the step).
 """
 from __future__ import annotations
 
@@ -285,6 +287,23 @@ SHARD_SHAPES = [(8192, 8192), (8192, 28672), (28672, 8192), (8192, 128256)]  # (
 SHARD_MS = (1, 32)
 
 
+def t3_compressed(K: int, N: int, seed: int, dev):
+    """BASELINE config 5 weights: Student-t (3 degrees of freedom) scaled to std
+    0.02, fp16, compressed on the device (same seed on every rank)."""
+    from spectra_b200 import compress as C
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.empty(N, K, dtype=torch.float16, device=dev)
+    for r0 in range(0, N, 16384):  # bounded temporaries
+        n = min(16384, N - r0)
+        z = torch.randn(4, n, K, generator=g, device=dev)
+        t = z[0] / torch.sqrt((z[1] ** 2 + z[2] ** 2 + z[3] ** 2) / 3.0)  # Student-t, df = 3
+        w[r0:r0 + n] = (t * (0.02 / 3.0 ** 0.5)).to(torch.float16)  # var(t_3) = 3
+        del z, t
+    c = C.compress_linear(w)
+    del w
+    return c
+
+
 def sharded_sweep(world: int, dev) -> dict:
     """BASELINE config 5 at the job's world size: each Llama-3-70B linear
     column-sharded over the ranks (``spectra_b200.sharded.ShardedW4A16Linear``:
@@ -295,18 +314,11 @@ def sharded_sweep(world: int, dev) -> dict:
     barrier as CUDA-graph replays of one rotation (all-gathers included), CUDA
     events around the whole run, slowest rank counted."""
     import copy as _copy
-    from spectra_b200 import compress as C
     from spectra_b200.sharded import ShardedW4A16Linear
     res = []
     for K, N in SHARD_SHAPES:
-        g = torch.Generator(device=dev).manual_seed(5000 + K + N)
-        z = torch.randn(4, N, K, generator=g, device=dev)
-        t = z[0] / torch.sqrt((z[1] ** 2 + z[2] ** 2 + z[3] ** 2) / 3.0)  # Student-t, df = 3
-        del z
-        w = (t * (0.02 / 3.0 ** 0.5)).to(torch.float16)  # var(t_3) = 3
-        del t
-        c = C.compress_linear(w)
-        del w
+        g = torch.Generator(device=dev).manual_seed(5000 + K + N + 1)
+        c = t3_compressed(K, N, 5000 + K + N, dev)
         n_out = c.outlier_idx.numel()
         lin = ShardedW4A16Linear(c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w, None,
                                  marlin_layout=True, device=dev)
@@ -346,6 +358,234 @@ def sharded_sweep(world: int, dev) -> dict:
     return {"gpus": world, "sharding": f"N-columns over {world} GPU(s), NCCL all-gather" if world > 1
             else "1 GPU (no collective)", "l2": "each rank rotates over shard copies > 3 x L2",
             "unit": "GB/s of the whole layer's algorithmic bytes; TFLOP/s for M > 1", "results": res}
+
+
+LLAMA3_8B = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                 num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=8192,
+                 rope_theta=500000.0, rms_norm_eps=1e-5, tie_word_embeddings=False,
+                 bos_token_id=None, eos_token_id=None, pad_token_id=None)
+
+
+def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256) -> dict:
+    """BASELINE config 4 at 1 GPU: a random-initialised Llama-3-8B (Hugging
+    Face skeleton, N(0, 0.02) init) with every linear and the embedding
+    compressed on the device into SPECTRA's format and bound to this package's
+    operator modules (``spectra_b200.modules``); a prompt of ``prompt_len``
+    uniform-random token ids, then ``new_tokens`` greedy tokens decoded the way
+    the reference engine's generate() does on a CUDA device
+    (spectra/engine.py:1762-1848): prefill with logits_to_keep=1 into a
+    StaticCache, then one decode step captured in a CUDA graph and replayed per
+    token, the logits' argmax read back to the host every token."""
+    from transformers import LlamaConfig, LlamaForCausalLM, StaticCache
+    from spectra_b200.modules import quantize_model
+    cfg = LlamaConfig(**LLAMA3_8B)
+    cfg.torch_dtype = torch.bfloat16
+    torch.manual_seed(0)
+    t0 = time.time()
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+    quantize_model(model)
+    model.eval()
+    build_s = time.time() - t0
+    wbytes = sum(b.numel() * b.element_size() for b in model.buffers()) + \
+        sum(p.numel() * p.element_size() for p in model.parameters())
+    g = torch.Generator(device=dev).manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=g, device=dev)
+    cache = StaticCache(config=cfg, max_cache_len=prompt_len + new_tokens)
+    if hasattr(cache, "early_initialization"):
+        cache.early_initialization(batch_size=1, num_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                                   dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        # prefill (the GEMM path; the lm_head sees one token)
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = model(ids, past_key_values=cache, cache_position=torch.arange(prompt_len, device=dev),
+                    use_cache=True, logits_to_keep=1)
+        b.record()
+        b.synchronize()
+        prefill_s = a.elapsed_time(b) / 1e3
+        tokens = [int(out.logits[:, -1, :].argmax(-1))]
+        static_in = torch.tensor([[tokens[0]]], device=dev)
+        static_pos = torch.tensor([prompt_len], device=dev)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                static_out = model(static_in, past_key_values=cache, cache_position=static_pos, use_cache=True)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            static_out = model(static_in, past_key_values=cache, cache_position=static_pos, use_cache=True)
+        torch.cuda.synchronize(dev)
+        t1 = time.perf_counter()
+        a.record()
+        for step in range(new_tokens - 1):
+            static_pos.fill_(prompt_len + step)
+            graph.replay()
+            nxt = static_out.logits[:, -1, :].argmax(-1, keepdim=True)
+            tokens.append(int(nxt.item()))
+            static_in.copy_(nxt)
+        b.record()
+        b.synchronize()
+        decode_s = a.elapsed_time(b) / 1e3
+        wall_s = time.perf_counter() - t1
+    del graph, static_out, cache, model
+    torch.cuda.empty_cache()
+    return {"model": "Llama-3-8B (random init N(0,0.02), every linear and the embedding in SPECTRA's format)",
+            "prompt_tokens": prompt_len, "new_tokens": new_tokens, "batch": 1,
+            "decode_tok_s": round((new_tokens - 1) / decode_s, 2), "ms_per_token": round(decode_s / (new_tokens - 1) * 1e3, 4),
+            "prefill_tok_s": round(prompt_len / prefill_s, 1), "decode_wall_s": round(wall_s, 4),
+            "weights_bytes": int(wbytes), "build_s": round(build_s, 1), "first_tokens": tokens[:8],
+            "how": "HF Llama skeleton + spectra_b200.modules (GEMV per linear at M=1, GEMM in prefill); "
+                   "StaticCache; one CUDA graph per decode step replayed 255 times; argmax read back every "
+                   "token as the engine's decode loop does; CUDA events around prefill and around the decode loop"}
+
+
+METRIC_SHARDED = ("W4A16 GEMV GB/s at M=1, Llama-3-70B linears column-sharded over the job's GPUs "
+                  "(8192x8192, 8192x28672, 28672x8192, 8192x128256 lm_head)")
+WORKLOAD_SHARDED = ("Llama-3-70B linears at M=1 (BASELINE config 5: Student-t weights), N-column-sharded "
+                    "over the job's GPUs, one NCCL all-gather per linear")
+
+
+def sharded_step_layers(world: int, dev):
+    """The four config-5 linears, sharded over the job's ranks, each rank keeping
+    several copies of its shards (> 3 x L2 in total) to rotate over."""
+    import copy as _copy
+    from spectra_b200.sharded import ShardedW4A16Linear
+    sets, nbytes, n_outs = [], 0, []
+    for K, N in SHARD_SHAPES:
+        c = t3_compressed(K, N, 5000 + K + N, dev)
+        n_outs.append(c.outlier_idx.numel())
+        nbytes += algorithmic_bytes(1, N, K, c.outlier_idx.numel())
+        lin = ShardedW4A16Linear(c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w, None,
+                                 marlin_layout=True, device=dev)
+        del c
+        torch.cuda.empty_cache()
+        sets.append(lin)
+    shard_bytes = sum(algorithmic_bytes(0, l_.rows, l_.in_features, n) for l_, n in zip(sets, n_outs))
+    copies = [sets]
+    while len(copies) < 16 and len(copies) * shard_bytes < 3 * 126e6:
+        cp = []
+        for lin in sets:
+            cl = _copy.copy(lin)
+            cl.packed, cl.scales, cl.zeros = lin.packed.clone(), lin.scales.clone(), lin.zeros.clone()
+            cl.outlier_w = None if lin.outlier_w is None else lin.outlier_w.clone()
+            cl._local_bufs = {}
+            cp.append(cl)
+        copies.append(cp)
+    return copies, nbytes
+
+
+def run_sharded(args, world, rank, local):
+    """N > 1: the headline is BASELINE config 5 strong-scaled -- the four
+    Llama-3-70B linears at M = 1, each column-sharded over the N ranks
+    (``ShardedW4A16Linear``: this rank's rows on the GEMV, one NCCL all-gather).
+    A step = the four sharded linears; value = the four layers' algorithmic
+    bytes x steps / the slowest rank's device time."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    copies, bytes_step = sharded_step_layers(world, dev)
+    g = torch.Generator(device=dev).manual_seed(99)
+    xs = {K: torch.randn(1, K, generator=g, device=dev).to(torch.bfloat16) for K in {k for k, _ in SHARD_SHAPES}}
+
+    def step(i):
+        for lin in copies[i % len(copies)]:
+            lin.forward(xs[lin.in_features])
+    for i in range(len(copies)):  # first calls: per-shape buffers, workspaces
+        step(i)
+    barrier(world)
+    timed = capture(lambda: [step(i) for i in range(args.steps)], dev)
+    warm = capture(lambda: [step(i) for i in range(max(args.warmup, 1))], dev)
+    clk = ClockSampler(local)
+    clk.start()
+    time.sleep(0.3)
+    warm.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    w0 = time.time()
+    dt = time_events(lambda: timed.replay(), dev)
+    w1 = time.time()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    dt_max = max_over_ranks(dt, world, dev)
+    value = bytes_step * args.steps / dt_max / 1e9
+
+    # all-gathers alone: their share of the step (same shapes, no GEMV)
+    import torch.distributed as dist
+    bufs = [(torch.zeros(lin.ns, dtype=torch.bfloat16, device=dev),
+             torch.empty(world * lin.ns, dtype=torch.bfloat16, device=dev)) for lin in copies[0]]
+    gat = capture(lambda: [[dist.all_gather_into_tensor(o, i_) for i_, o in bufs] for _ in range(args.steps)], dev)
+    gat.replay()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    dt_g = max_over_ranks(time_events(lambda: gat.replay(), dev), world, dev)
+
+    # end to end through the public module: the step's activations from pinned
+    # host memory, all four outputs back to the host, every step
+    h_x = {K: x.cpu().pin_memory() for K, x in xs.items()}
+    out_n = sum(l_.N for l_ in copies[0])
+    h_out = torch.empty(out_n, dtype=torch.bfloat16).pin_memory()
+    d_out = torch.empty(out_n, dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        for K, hx in h_x.items():
+            xs[K].copy_(hx, non_blocking=True)
+        off = 0
+        for lin in copies[i % len(copies)]:
+            y = lin.forward(xs[lin.in_features])
+            d_out[off:off + lin.N].copy_(y.reshape(-1))
+            off += lin.N
+        h_out.copy_(d_out, non_blocking=True)
+    e2e_graphable = capture(lambda: [e2e_step(i) for i in range(args.steps)], dev)
+    e2e_graphable.replay()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    dt_e2e = max_over_ranks(time_events(lambda: e2e_graphable.replay(), dev), world, dev)
+    # roofline of the dominant kernel: this rank's lm_head shard GEMV alone
+    from spectra_b200 import kernels as SK
+    heads = [cp[-1] for cp in copies]
+    x_h = xs[heads[0].in_features]
+    outs_h = [torch.empty(1, heads[0].rows, dtype=torch.bfloat16, device=dev) for _ in heads]
+    g_h = capture(lambda: [SK.fused_w4a16_gemv_hdsq(x_h, h.packed, h.scales, h.zeros, outlier_idx=h.outlier_idx,
+                                                    outlier_w=h.outlier_w, out=o, marlin_layout=True)
+                           for h, o in zip(heads, outs_h)], dev)
+    for _ in range(3):
+        g_h.replay()
+    dt_h = time_events(lambda: [g_h.replay() for _ in range(5)], dev) / (5 * len(heads))
+    h_bytes = algorithmic_bytes(1, heads[0].rows, heads[0].in_features, heads[0].outlier_idx.numel())
+    peak, peak_kind = measured_peaks()
+    clk.stop()
+    h2d = sum(x.numel() * 2 for x in h_x.values())
+    if rank == 0:
+        line = {
+            "metric": METRIC_SHARDED, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: Student-t(3) weights scaled to std 0.02, fp16, quantised on device by "
+                    "spectra_b200.compress; N(0,1) bf16 activations",
+            "config": {"workload": WORKLOAD_SHARDED, "bytes_per_step": bytes_step,
+                       "shard_copies": len(copies), "l2": "each rank rotates over shard copies > 3 x L2",
+                       "graphs": "the timed steps (GEMVs and all-gathers) replayed as one CUDA graph",
+                       "parallelism": f"N-column sharding over {world} GPUs (NCCL all-gather)"},
+            "allgather": {"us_per_step": round(dt_g / args.steps * 1e6, 3),
+                          "share_of_step": round(dt_g / dt_max, 4),
+                          "what": "the step's four all-gathers alone (same shapes), CUDA graph, max over ranks"},
+            "e2e": {"value": round(bytes_step * args.steps / dt_e2e / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_n * 2,
+                    "how": "ShardedW4A16Linear.forward per linear captured in a CUDA graph with a pinned H2D of "
+                           "the activations and a D2H of all four outputs every step"},
+            "gpu_launches": 4 * args.steps * 2,
+            "roofline": {"bound": "hbm", "achieved": round(h_bytes / dt_h / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(h_bytes / dt_h / 1e9 / peak, 4), "traffic": None,
+                         "kernel": f"gemv_pf_kernel lm_head shard K=8192 N={heads[0].rows} M=1 (rank 0)",
+                         "peak_source": peak_kind, "avg_launch_us": round(dt_h * 1e6, 3)},
+            "clocks": clk.summary(w0, w1),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    del timed, warm, gat, e2e_graphable, g_h
 
 
 def measured_peaks():
@@ -407,9 +647,58 @@ def cpu_baseline(budget_s: float = 12.0) -> dict:
                       f"(torch dequant + fp32 matmul, oracle/cpu_path.py), {total_t:.1f} s"}
 
 
+def run_reference_sharded(args, world):
+    """--impl reference at N > 1: the reference's CPU formula on the config-5
+    linears (the workload our arm shards), timed on a bounded row sample."""
+    import numpy as np
+    from oracle import cpu_path
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(5)
+    frac = 0.01
+    mats = []
+    for K, N in SHARD_SHAPES:
+        n = max(16, int(N * frac))
+        n_out = max(1, int(round(K * 0.02)))
+        p = torch.from_numpy(rng.integers(0, 256, size=(n, K // 2), dtype=np.uint8))
+        sc = torch.from_numpy(rng.uniform(0.002, 0.02, size=(n, K // 32)).astype(np.float16))
+        z = torch.from_numpy(rng.integers(0, 16, size=(n, K // 32), dtype=np.uint8))
+        idx = torch.from_numpy(np.sort(rng.choice(K, size=n_out, replace=False)).astype(np.int64))
+        ow = torch.from_numpy(rng.normal(0, 0.05, size=(n, n_out)).astype(np.float16))
+        x = torch.randn(1, K).to(torch.bfloat16)
+        mats.append((x, p, sc, z, idx, ow, algorithmic_bytes(1, n, K, n_out)))
+
+    def one():
+        t0 = time.perf_counter()
+        for x, p, sc, z, idx, ow, _ in mats:
+            cpu_path.linear(x, p, sc, z, idx, ow, marlin=True)
+        return sum(m[-1] for m in mats), time.perf_counter() - t0
+    for _ in range(args.warmup):
+        one()
+    nbytes, secs = 0, 0.0
+    for _ in range(args.steps):
+        b, t = one()
+        nbytes += b
+        secs += t
+    v = nbytes / secs / 1e9
+    sample = (f"each step: {frac * 100:.1f}% of the rows of each of the four config-5 linears (random codes of "
+              f"that shape) through the reference's CPU formula (oracle/cpu_path.py)")
+    line = {"impl": "reference", "metric": METRIC_SHARDED, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random SPECTRA-format codes of the config-5 shapes; N(0,1) activations)",
+            "config": {"workload": WORKLOAD_SHARDED},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU formula on the host cores."""
     if rank != 0:
+        return
+    if world > 1:
+        run_reference_sharded(args, world)
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -563,6 +852,7 @@ def run_gpu(args, world, rank, local):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
+    cfg4 = config4_decode(dev) if (not args.no_config4 and world == 1) else None
     shard = sharded_sweep(world, dev) if not args.no_sharded_sweep else None
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
@@ -595,6 +885,7 @@ def run_gpu(args, world, rank, local):
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": cpu,
             "gemm_sweep": sweep,
+            "config4_decode": cfg4,
             "sharded_sweep": shard,
         }
         print(json.dumps(line), flush=True)
@@ -610,6 +901,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the config-3 GEMM/GEMV shape sweep")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the config-4 Llama-3-8B greedy decode (tok/s at 1 GPU)")
     ap.add_argument("--no-sharded-sweep", action="store_true",
                     help="skip the config-5 column-sharded Llama-3-70B layer sweep")
     args = ap.parse_args()
@@ -617,6 +910,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif world > 1:
+            run_sharded(args, world, rank, local)
         else:
             run_gpu(args, world, rank, local)
     finally:
