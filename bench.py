@@ -366,7 +366,7 @@ LLAMA3_8B = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, n
                  bos_token_id=None, eos_token_id=None, pad_token_id=None)
 
 
-def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256) -> dict:
+def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256, compile_model: bool = False) -> dict:
     """BASELINE config 4 at 1 GPU: a random-initialised Llama-3-8B (Hugging
     Face skeleton, N(0, 0.02) init) with every linear and the embedding
     compressed on the device into SPECTRA's format and bound to this package's
@@ -386,16 +386,26 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256) -> dict:
         model = LlamaForCausalLM(cfg).to(torch.bfloat16)
     quantize_model(model)
     model.eval()
+    if compile_model:  # as the reference engine's loader does (spectra/engine.py:1240-1251)
+        model = torch.compile(model, mode="default", dynamic=True)
     build_s = time.time() - t0
     wbytes = sum(b.numel() * b.element_size() for b in model.buffers()) + \
         sum(p.numel() * p.element_size() for p in model.parameters())
     g = torch.Generator(device=dev).manual_seed(4)
     ids = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=g, device=dev)
-    cache = StaticCache(config=cfg, max_cache_len=prompt_len + new_tokens)
+    # transformers' StaticLayer appends at its own running count, so the three
+    # warm-up passes before capture take three slots: room for them, or the
+    # last decode steps would index past the cache
+    cache = StaticCache(config=cfg, max_cache_len=prompt_len + new_tokens + 8)  # (slot count rewound below)
     if hasattr(cache, "early_initialization"):
         cache.early_initialization(batch_size=1, num_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
                                    dtype=torch.bfloat16, device=dev)
     with torch.no_grad():
+        # one untimed prefill first (first-call costs: lazy cache allocation,
+        # kernel attributes, compilation when enabled), then a clean cache
+        model(ids, past_key_values=cache, cache_position=torch.arange(prompt_len, device=dev), use_cache=True,
+              logits_to_keep=1)
+        cache.reset()
         # prefill (the GEMM path; the lm_head sees one token)
         torch.cuda.synchronize(dev)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -418,6 +428,11 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256) -> dict:
         with torch.cuda.graph(graph, stream=s):
             static_out = model(static_in, past_key_values=cache, cache_position=static_pos, use_cache=True)
         torch.cuda.synchronize(dev)
+        # the warm-up passes advanced transformers' running slot count: rewind it
+        # so every replayed step writes its own key/value slot
+        for layer in getattr(cache, "layers", []):
+            if isinstance(getattr(layer, "cumulative_length", None), torch.Tensor):
+                layer.cumulative_length.fill_(prompt_len)
         t1 = time.perf_counter()
         a.record()
         for step in range(new_tokens - 1):
@@ -437,6 +452,7 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256) -> dict:
             "decode_tok_s": round((new_tokens - 1) / decode_s, 2), "ms_per_token": round(decode_s / (new_tokens - 1) * 1e3, 4),
             "prefill_tok_s": round(prompt_len / prefill_s, 1), "decode_wall_s": round(wall_s, 4),
             "weights_bytes": int(wbytes), "build_s": round(build_s, 1), "first_tokens": tokens[:8],
+            "compiled": bool(compile_model),
             "how": "HF Llama skeleton + spectra_b200.modules (GEMV per linear at M=1, GEMM in prefill); "
                    "StaticCache; one CUDA graph per decode step replayed 255 times; argmax read back every "
                    "token as the engine's decode loop does; CUDA events around prefill and around the decode loop"}
@@ -852,7 +868,7 @@ def run_gpu(args, world, rank, local):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
-    cfg4 = config4_decode(dev) if (not args.no_config4 and world == 1) else None
+    cfg4 = config4_decode(dev, compile_model=args.config4_compile) if (not args.no_config4 and world == 1) else None
     shard = sharded_sweep(world, dev) if not args.no_sharded_sweep else None
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
@@ -903,6 +919,9 @@ def main():
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the config-3 GEMM/GEMV shape sweep")
     ap.add_argument("--no-config4", action="store_true",
                     help="skip the config-4 Llama-3-8B greedy decode (tok/s at 1 GPU)")
+    ap.add_argument("--config4-compile", action="store_true",
+                    help="compile the config-4 model's non-linear parts with torch.compile, as the reference "
+                         "engine's loader does (adds the compilation time to the run)")
     ap.add_argument("--no-sharded-sweep", action="store_true",
                     help="skip the config-5 column-sharded Llama-3-70B layer sweep")
     args = ap.parse_args()

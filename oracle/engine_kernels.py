@@ -8,9 +8,11 @@ and the GPU engine test compares this package's kernels with it.
 
 Both functions keep the reference wrappers' signatures and output-dtype
 rules (spectra/kernels.py:132-184, :333-389) and compute with the dequant
-formula of the reference's unit test (tests/test_kernels.py:31-39): exact
-``(q - z) * s`` in fp32, fp32 matmul, outlier columns added from the exact
-outlier weights, one rounding at the end.
+formula of the reference's unit test (tests/test_kernels.py:31-39), exact
+``(q - z) * s`` in fp32: the GEMV multiplies the exact weights and
+activations in fp32 (the reference GEMV's arithmetic), the GEMM the operands
+rounded to the compute dtype (the reference GEMM's tensor-core operands);
+both accumulate in fp32 and round once at the end.
 """
 from __future__ import annotations
 
@@ -40,10 +42,16 @@ def fused_w4a16_gemv_hdsq(x: torch.Tensor, packed_w: torch.Tensor, scales: torch
 def batched_w4a16_gemm(a: torch.Tensor, packed_b: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                        outlier_idx: Optional[torch.Tensor] = None, outlier_w: Optional[torch.Tensor] = None,
                        marlin_layout: bool = False) -> torch.Tensor:
+    """The reference GEMM feeds its tensor-core dot the dequantised weights,
+    the activations and the outlier weights rounded to the compute dtype (bf16
+    for bf16 activations, else fp16; spectra/kernels.py:256-261, :315-317)."""
     K = a.shape[-1]
-    a2 = a.reshape(-1, K)
-    c = cpu_path.linear(a2, packed_b, scales, zeros, outlier_idx, outlier_w, None, marlin=marlin_layout)
     compute = torch.bfloat16 if a.dtype == torch.bfloat16 else torch.float16
+    a2 = a.reshape(-1, K).to(compute).float()
+    w = cpu_path.dequant(packed_b, scales, zeros, marlin_layout).to(compute).float()
+    c = a2 @ w.t()
+    if outlier_idx is not None and outlier_w is not None and outlier_idx.numel():
+        c = c + a2[:, outlier_idx] @ outlier_w.to(compute).float().t()
     return c.to(compute).reshape(a.shape[:-1] + (packed_b.shape[0],)).to(a.dtype)
 
 

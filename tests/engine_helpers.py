@@ -5,6 +5,7 @@ files exist for a random model), and the injection of an operator module as
 binds this package in place of the reference's Triton kernels."""
 from __future__ import annotations
 
+import hashlib
 import sys
 import types
 from pathlib import Path
@@ -49,6 +50,11 @@ class IdTokenizer:
 
     def convert_tokens_to_ids(self, name):
         raise KeyError(name)
+
+
+def sha256(t: torch.Tensor) -> str:
+    """sha256 of a tensor's bytes (contiguous, on the host)."""
+    return hashlib.sha256(t.detach().contiguous().cpu().view(torch.uint8).numpy().tobytes()).hexdigest()
 
 
 def prompt_ids(seed: int = 11):

@@ -5,6 +5,9 @@
 * tiny_llama.trdc  -- its random-initialised weights (seed 1234) compressed by
                       the reference's own SpectraCompressor (container
                       TRDC4B01, spectra/compressor.py:393-571);
+* bound_tensors.json -- sha256 of every tensor the reference engine's loader
+                      bound to its quantised modules (packed codes, scales,
+                      unpacked zero points, int64 outlier indices, outlier weights);
 * engine_golden.npz -- the reference engine (spectra/engine.py) loading that
                       container on the CPU, with the reference's operator API
                       restated in torch (oracle/engine_kernels.py) injected as
@@ -60,6 +63,18 @@ def main() -> None:
 
     engine = E.SpectraUniversalEngine.load(str(H.TINY_TRDC), model_dir=str(H.TINY_DIR), device_index=0)
     engine.tokenizer = H.IdTokenizer()
+    # what the reference loader bound to each quantised module (sha256 of the
+    # buffers SpectraFusedLinear / SpectraFusedEmbedding received)
+    bound = {}
+    for mname, mod in engine.model.named_modules():
+        if isinstance(mod, (E.SpectraFusedLinear, E.SpectraFusedEmbedding)):
+            rec = {k: H.sha256(getattr(mod, a)) for k, a in (("packed", "packed_weight"), ("scales", "scales"),
+                                                             ("zeros", "zeros"), ("outlier_idx", "outlier_idx"),
+                                                             ("outlier_w", "outlier_weight"))
+                   if getattr(mod, a, None) is not None}
+            rec["marlin_layout"] = bool(mod.marlin_layout)
+            bound[mname + ".weight"] = rec
+    (H.TINY_DIR / "bound_tensors.json").write_text(json.dumps(bound, indent=1, sort_keys=True))
     ids = H.prompt_ids()
     toks, res = H.greedy(engine, ids)
     assert len(toks) == H.NEW_TOKENS, toks

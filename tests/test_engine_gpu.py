@@ -12,8 +12,14 @@ Checks:
   * teacher-forced logits of the whole sequence: ours vs the torch restatement
     on the same GPU within 1e-2*||logits||_inf, and vs the reference engine's
     own CPU run (golden fixture) within 5e-2*||logits||_inf;
-  * greedy tokens equal the fixture's wherever the fixture's top-1 margin
-    exceeds the numerical noise (random-init logits have near-ties).
+  * the eager decode loop's greedy tokens equal the fixture's wherever the
+    fixture's top-1 margin exceeds the numerical noise (random-init logits
+    have near-ties), and ours equal the torch restatement's on both paths.
+The CUDA-graph decode is compared with the torch restatement only: with
+transformers 5.x the engine's three warm-up passes before capture
+(spectra/engine.py:2101-2108) advance the StaticCache's own slot counter, so
+its graph path attends to shifted key/value slots and chooses other tokens
+than its eager path -- identically with either operator module.
 The engine runs in a child process: importing it compiles the model with
 torch.compile and sets process-wide options."""
 import json
@@ -53,7 +59,9 @@ def _gold():
 def test_engine_used_our_kernels_on_both_paths(result):
     assert result["plan"] == "FULL_GPU_RESIDENT"
     calls = result["ours_calls"]
-    assert calls["gemv"] > 0 and calls["gemm"] > 0, calls
+    graph_calls = result["ours_graph_calls"]
+    assert graph_calls["gemv"] > 0 and graph_calls["gemm"] > 0, graph_calls
+    assert calls["gemv"] > graph_calls["gemv"] and calls["gemm"] > graph_calls["gemm"], calls
     assert result["ours_graph"] is True          # CUDA-graph decode captured our launches
     assert result["ours_eager_graph"] is False   # and the eager decode loop ran them too
     assert result["calls_after_oracle"] == calls  # the oracle run used none of ours
@@ -77,7 +85,7 @@ def test_logits_match_the_reference_engine_on_cpu(result):
     assert np.max(np.abs(ours - gold)) <= 5e-2 * np.max(np.abs(gold))
 
 
-@pytest.mark.parametrize("tag", ["ours", "ours_eager", "oracle"])
+@pytest.mark.parametrize("tag", ["ours_eager", "oracle_eager"])
 def test_greedy_tokens_match_where_the_choice_is_clear(result, tag):
     g = _gold()
     gold_toks = g["tokens"].tolist()
@@ -95,12 +103,7 @@ def test_greedy_tokens_match_where_the_choice_is_clear(result, tag):
         break  # later tokens follow a different prefix
 
 
-def test_ours_and_torch_restatement_choose_the_same_tokens(result):
-    assert result["ours_tokens"] == result["ours_eager_tokens"]
-    ours, ref = result["ours_tokens"], result["oracle_tokens"]
-    if ours != ref:
-        i = next(k for k, (a, b) in enumerate(zip(ours, ref)) if a != b)
-        row = _logits(result, "oracle")[H.PROMPT_LEN - 1 + i] if i < H.NEW_TOKENS - 1 else None
-        assert row is not None
-        top2 = np.sort(row)[-2:]
-        assert top2[1] - top2[0] <= 1e-2 * np.max(np.abs(_logits(result, "oracle")))
+@pytest.mark.parametrize("path", ["", "_eager"])
+def test_ours_and_torch_restatement_choose_the_same_tokens(result, path):
+    assert result["oracle" + path + "_graph"] is (path == "")
+    assert result["ours" + path + "_tokens"] == result["oracle" + path + "_tokens"]
