@@ -386,8 +386,13 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256, compile_m
         model = LlamaForCausalLM(cfg).to(torch.bfloat16)
     quantize_model(model)
     model.eval()
+    compiled = False
     if compile_model:  # as the reference engine's loader does (spectra/engine.py:1240-1251)
-        model = torch.compile(model, mode="default", dynamic=True)
+        try:
+            model = torch.compile(model, mode="default", dynamic=True)
+            compiled = True
+        except Exception:  # noqa: BLE001 -- the engine also falls back to eager on any failure
+            compiled = False
     build_s = time.time() - t0
     wbytes = sum(b.numel() * b.element_size() for b in model.buffers()) + \
         sum(p.numel() * p.element_size() for p in model.parameters())
@@ -403,8 +408,16 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256, compile_m
     with torch.no_grad():
         # one untimed prefill first (first-call costs: lazy cache allocation,
         # kernel attributes, compilation when enabled), then a clean cache
-        model(ids, past_key_values=cache, cache_position=torch.arange(prompt_len, device=dev), use_cache=True,
-              logits_to_keep=1)
+        try:
+            model(ids, past_key_values=cache, cache_position=torch.arange(prompt_len, device=dev), use_cache=True,
+                  logits_to_keep=1)
+        except Exception:  # noqa: BLE001 -- compilation failed at its first call: run eager
+            if not compiled:
+                raise
+            model = model._orig_mod
+            compiled = False
+            model(ids, past_key_values=cache, cache_position=torch.arange(prompt_len, device=dev), use_cache=True,
+                  logits_to_keep=1)
         cache.reset()
         # prefill (the GEMM path; the lm_head sees one token)
         torch.cuda.synchronize(dev)
@@ -452,7 +465,7 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256, compile_m
             "decode_tok_s": round((new_tokens - 1) / decode_s, 2), "ms_per_token": round(decode_s / (new_tokens - 1) * 1e3, 4),
             "prefill_tok_s": round(prompt_len / prefill_s, 1), "decode_wall_s": round(wall_s, 4),
             "weights_bytes": int(wbytes), "build_s": round(build_s, 1), "first_tokens": tokens[:8],
-            "compiled": bool(compile_model),
+            "compiled": compiled,
             "how": "HF Llama skeleton + spectra_b200.modules (GEMV per linear at M=1, GEMM in prefill); "
                    "StaticCache; one CUDA graph per decode step replayed 255 times; argmax read back every "
                    "token as the engine's decode loop does; CUDA events around prefill and around the decode loop"}
@@ -868,7 +881,7 @@ def run_gpu(args, world, rank, local):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
-    cfg4 = config4_decode(dev, compile_model=args.config4_compile) if (not args.no_config4 and world == 1) else None
+    cfg4 = config4_decode(dev, compile_model=not args.config4_eager) if (not args.no_config4 and world == 1) else None
     shard = sharded_sweep(world, dev) if not args.no_sharded_sweep else None
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
@@ -919,9 +932,9 @@ def main():
     ap.add_argument("--no-gemm-sweep", action="store_true", help="skip the config-3 GEMM/GEMV shape sweep")
     ap.add_argument("--no-config4", action="store_true",
                     help="skip the config-4 Llama-3-8B greedy decode (tok/s at 1 GPU)")
-    ap.add_argument("--config4-compile", action="store_true",
-                    help="compile the config-4 model's non-linear parts with torch.compile, as the reference "
-                         "engine's loader does (adds the compilation time to the run)")
+    ap.add_argument("--config4-eager", action="store_true",
+                    help="run the config-4 model eagerly instead of compiling its non-linear parts with "
+                         "torch.compile as the reference engine's loader does")
     ap.add_argument("--no-sharded-sweep", action="store_true",
                     help="skip the config-5 column-sharded Llama-3-70B layer sweep")
     args = ap.parse_args()
