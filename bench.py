@@ -238,7 +238,7 @@ def time_events(fn, dev) -> float:
 
 
 GEMM_SHAPES = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]  # (K, N)
-GEMM_MS = (16, 64, 256)
+GEMM_MS = (2, 4, 8, 16, 64, 256)  # 16-256: BASELINE config 3; 2-8: the engine's generate_batch sizes
 
 
 def gemm_sweep(SK, dev) -> dict:
@@ -304,10 +304,10 @@ def t3_compressed(K: int, N: int, seed: int, dev):
     return c
 
 
-def sharded_sweep(world: int, dev) -> dict:
+def sharded_sweep(world: int, dev, exchange: str = "auto") -> dict:
     """BASELINE config 5 at the job's world size: each Llama-3-70B linear
     column-sharded over the ranks (``spectra_b200.sharded.ShardedW4A16Linear``:
-    this rank's rows with the production kernels, one NCCL all-gather), weights
+    this rank's rows with the production kernels, one all-gather), weights
     heavy-tailed (Student-t, 3 degrees of freedom, scaled to std 0.02, the same
     seed on every rank) and quantised on the device.  Each rank rotates over
     copies of its shard totalling > 3 x L2; calls run back to back after one
@@ -321,7 +321,7 @@ def sharded_sweep(world: int, dev) -> dict:
         c = t3_compressed(K, N, 5000 + K + N, dev)
         n_out = c.outlier_idx.numel()
         lin = ShardedW4A16Linear(c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w, None,
-                                 marlin_layout=True, device=dev)
+                                 marlin_layout=True, device=dev, exchange=exchange)
         del c
         shard_bytes = algorithmic_bytes(0, lin.rows, K, n_out)
         lins = [lin]
@@ -329,6 +329,7 @@ def sharded_sweep(world: int, dev) -> dict:
             cl = _copy.copy(lin)
             cl.packed, cl.scales, cl.zeros = lin.packed.clone(), lin.scales.clone(), lin.zeros.clone()
             cl.outlier_w = None if lin.outlier_w is None else lin.outlier_w.clone()
+            cl._local_bufs, cl._exchanges = {}, {}
             lins.append(cl)
         torch.cuda.empty_cache()
         for M in SHARD_MS:
@@ -353,9 +354,12 @@ def sharded_sweep(world: int, dev) -> dict:
             if M > 1:
                 r["tflops"] = round(2.0 * M * N * (K + n_out) / dt / 1e12, 2)
             res.append(r)
+        for l_ in lins:
+            l_.close()
         del lin, lins
         torch.cuda.empty_cache()
-    return {"gpus": world, "sharding": f"N-columns over {world} GPU(s), NCCL all-gather" if world > 1
+    exch = ("NVLink peer-memory all-gather" if exchange != "collective" else "NCCL all-gather")
+    return {"gpus": world, "sharding": f"N-columns over {world} GPU(s), {exch}" if world > 1
             else "1 GPU (no collective)", "l2": "each rank rotates over shard copies > 3 x L2",
             "unit": "GB/s of the whole layer's algorithmic bytes; TFLOP/s for M > 1", "results": res}
 
@@ -477,7 +481,7 @@ WORKLOAD_SHARDED = ("Llama-3-70B linears at M=1 (BASELINE config 5: Student-t we
                     "over the job's GPUs, one NCCL all-gather per linear")
 
 
-def sharded_step_layers(world: int, dev):
+def sharded_step_layers(world: int, dev, exchange: str = "auto"):
     """The four config-5 linears, sharded over the job's ranks, each rank keeping
     several copies of its shards (> 3 x L2 in total) to rotate over."""
     import copy as _copy
@@ -488,7 +492,7 @@ def sharded_step_layers(world: int, dev):
         n_outs.append(c.outlier_idx.numel())
         nbytes += algorithmic_bytes(1, N, K, c.outlier_idx.numel())
         lin = ShardedW4A16Linear(c.packed, c.scales, c.zeros, c.outlier_idx, c.outlier_w, None,
-                                 marlin_layout=True, device=dev)
+                                 marlin_layout=True, device=dev, exchange=exchange)
         del c
         torch.cuda.empty_cache()
         sets.append(lin)
@@ -500,7 +504,7 @@ def sharded_step_layers(world: int, dev):
             cl = _copy.copy(lin)
             cl.packed, cl.scales, cl.zeros = lin.packed.clone(), lin.scales.clone(), lin.zeros.clone()
             cl.outlier_w = None if lin.outlier_w is None else lin.outlier_w.clone()
-            cl._local_bufs = {}
+            cl._local_bufs, cl._exchanges = {}, {}
             cp.append(cl)
         copies.append(cp)
     return copies, nbytes
@@ -509,12 +513,13 @@ def sharded_step_layers(world: int, dev):
 def run_sharded(args, world, rank, local):
     """N > 1: the headline is BASELINE config 5 strong-scaled -- the four
     Llama-3-70B linears at M = 1, each column-sharded over the N ranks
-    (``ShardedW4A16Linear``: this rank's rows on the GEMV, one NCCL all-gather).
+    (``ShardedW4A16Linear``: this rank's rows on the GEMV, one all-gather: the
+    NVLink peer-memory exchange kernel, or NCCL with ``--exchange collective``).
     A step = the four sharded linears; value = the four layers' algorithmic
     bytes x steps / the slowest rank's device time."""
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    copies, bytes_step = sharded_step_layers(world, dev)
+    copies, bytes_step = sharded_step_layers(world, dev, args.exchange)
     g = torch.Generator(device=dev).manual_seed(99)
     xs = {K: torch.randn(1, K, generator=g, device=dev).to(torch.bfloat16) for K in {k for k, _ in SHARD_SHAPES}}
 
@@ -541,15 +546,31 @@ def run_sharded(args, world, rank, local):
     dt_max = max_over_ranks(dt, world, dev)
     value = bytes_step * args.steps / dt_max / 1e9
 
-    # all-gathers alone: their share of the step (same shapes, no GEMV)
+    # the exchanges alone: their share of the step (same shapes, no GEMV) --
+    # the layers' own peer-memory exchanges when they use them, and NCCL's
+    # all-gather of the same slices for comparison
     import torch.distributed as dist
+    exchanges = [lin._exchanges.get(("y", 1, torch.bfloat16)) for lin in copies[0]]
+    dt_g = None
+    if all(e is not None for e in exchanges):
+        gat = capture(lambda: [[e.gather() for e in exchanges] for _ in range(args.steps)], dev)
+        gat.replay()
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        dt_g = max_over_ranks(time_events(lambda: gat.replay(), dev), world, dev)
+        del gat
     bufs = [(torch.zeros(lin.ns, dtype=torch.bfloat16, device=dev),
              torch.empty(world * lin.ns, dtype=torch.bfloat16, device=dev)) for lin in copies[0]]
     gat = capture(lambda: [[dist.all_gather_into_tensor(o, i_) for i_, o in bufs] for _ in range(args.steps)], dev)
     gat.replay()
     barrier(world)
     torch.cuda.synchronize(dev)
-    dt_g = max_over_ranks(time_events(lambda: gat.replay(), dev), world, dev)
+    dt_nccl = max_over_ranks(time_events(lambda: gat.replay(), dev), world, dev)
+    del gat
+    if dt_g is None:
+        dt_g = dt_nccl
+    exch_name = ("NVLink peer-memory all-gather kernel" if all(e is not None for e in exchanges)
+                 else "NCCL all-gather")
 
     # end to end through the public module: the step's activations from pinned
     # host memory, all four outputs back to the host, every step
@@ -586,6 +607,7 @@ def run_sharded(args, world, rank, local):
     h_bytes = algorithmic_bytes(1, heads[0].rows, heads[0].in_features, heads[0].outlier_idx.numel())
     peak, peak_kind = measured_peaks()
     clk.stop()
+    shard = sharded_sweep(world, dev, args.exchange) if not args.no_sharded_sweep else None
     h2d = sum(x.numel() * 2 for x in h_x.values())
     if rank == 0:
         line = {
@@ -597,10 +619,12 @@ def run_sharded(args, world, rank, local):
             "config": {"workload": WORKLOAD_SHARDED, "bytes_per_step": bytes_step,
                        "shard_copies": len(copies), "l2": "each rank rotates over shard copies > 3 x L2",
                        "graphs": "the timed steps (GEMVs and all-gathers) replayed as one CUDA graph",
-                       "parallelism": f"N-column sharding over {world} GPUs (NCCL all-gather)"},
+                       "parallelism": f"N-column sharding over {world} GPUs ({exch_name})"},
             "allgather": {"us_per_step": round(dt_g / args.steps * 1e6, 3),
                           "share_of_step": round(dt_g / dt_max, 4),
-                          "what": "the step's four all-gathers alone (same shapes), CUDA graph, max over ranks"},
+                          "nccl_us_per_step": round(dt_nccl / args.steps * 1e6, 3),
+                          "what": f"the step's four exchanges alone ({exch_name}; same shapes), CUDA graph, max "
+                                  "over ranks; nccl_us_per_step: NCCL all_gather_into_tensor of the same slices"},
             "e2e": {"value": round(bytes_step * args.steps / dt_e2e / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_n * 2,
                     "how": "ShardedW4A16Linear.forward per linear captured in a CUDA graph with a pinned H2D of "
@@ -612,9 +636,13 @@ def run_sharded(args, world, rank, local):
                          "peak_source": peak_kind, "avg_launch_us": round(dt_h * 1e6, 3)},
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": None,
+            "config5_sharded_layers": shard,
         }
         print(json.dumps(line), flush=True)
-    del timed, warm, gat, e2e_graphable, g_h
+    del timed, warm, e2e_graphable, g_h
+    for cp in copies:
+        for lin in cp:
+            lin.close()
 
 
 def measured_peaks():
@@ -935,6 +963,8 @@ def main():
     ap.add_argument("--config4-eager", action="store_true",
                     help="run the config-4 model eagerly instead of compiling its non-linear parts with "
                          "torch.compile as the reference engine's loader does")
+    ap.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
+                    help="N > 1: the sharded layers' all-gather (auto: the NVLink peer-memory exchange kernel)")
     ap.add_argument("--no-sharded-sweep", action="store_true",
                     help="skip the config-5 column-sharded Llama-3-70B layer sweep")
     args = ap.parse_args()

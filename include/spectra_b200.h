@@ -266,7 +266,7 @@ SPECTRA_API int spectra_w4a16_embedding(
  * index of the maximum of row m of x [M, N] (a NaN counts as the maximum, as
  * in torch.argmax); val[m] (optional) = that maximum as fp32.  idx_offset lets
  * an N-sharded lm_head report the layer's row index, so the shards reduce
- * (value, index) pairs instead of gathering every logit.
+ * (value, index) pairs instead of gathering every logit.  M <= 65535.
  */
 SPECTRA_API int spectra_argmax(const void* x, int x_dtype, int64_t x_row_stride, int64_t M, int64_t N,
                                int64_t idx_offset, int64_t* idx, float* val, void* stream);
@@ -280,6 +280,40 @@ SPECTRA_API int spectra_argmax(const void* x, int x_dtype, int64_t x_row_stride,
  */
 SPECTRA_API int spectra_fwht(const void* x, int x_dtype, int64_t x_row_stride, void* y, int y_dtype,
                              int64_t y_row_stride, int64_t M, int64_t n, int normalize, void* stream);
+
+/*
+ * All-gather of an N-sharded layer's output over NVLink peer memory (the
+ * reference has no multi-GPU path: this is the exchange step of its large
+ * layers column-sharded over the GPUs of one node, in place of an NCCL
+ * all-gather).  Setup, once per layer shape on every rank:
+ *   bytes = spectra_p2p_buffer_bytes(M, ns, elem_bytes, world);
+ *   spectra_p2p_alloc(bytes, &mine, handle);     -- cudaMalloc'd, zeroed (synchronises the device);
+ *                                                   64-byte CUDA IPC handle
+ *   (exchange the handles between the ranks, e.g. over the host's process group)
+ *   spectra_p2p_open(handle_of_r, &peer[r]);     -- for every r != rank; peer[rank] = mine
+ * and an int32[SPECTRA_P2P_STATE_INTS] device `state`, zeroed.  Per call, with this rank's slice
+ * [M][ns] (elem_bytes each, 16-byte aligned, spectra_p2p_buffer_bytes' slice
+ * rounded up to 16 bytes readable) in `src`: the launched kernel pushes it into
+ * every peer's buffer, exchanges an epoch flag with every peer and writes the
+ * gathered [M][N] output (row stride out_row_stride elements; rank r's columns
+ * start at r*ns, N <= world*ns: the last ranks' may be ragged or empty).
+ * All ranks must make the same calls in the same order; one call may be
+ * replayed from a CUDA graph.  A peer that does not signal within
+ * wait_limit_ns ends the wait: the event is counted by
+ * spectra_device_timeouts and the output is undefined.  Teardown:
+ * spectra_p2p_close(peer[r]) for r != rank, then spectra_p2p_free(mine).
+ * spectra_p2p_buffer_bytes returns -1 for an unsupported shape
+ * (elem_bytes 2, 4 or 8; world 1..8).
+ */
+#define SPECTRA_P2P_STATE_INTS 128
+SPECTRA_API int64_t spectra_p2p_buffer_bytes(int64_t M, int64_t ns, int64_t elem_bytes, int world);
+SPECTRA_API int spectra_p2p_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+SPECTRA_API int spectra_p2p_open(const void* ipc_handle, void** ptr);
+SPECTRA_API int spectra_p2p_close(void* ptr);
+SPECTRA_API int spectra_p2p_free(void* ptr);
+SPECTRA_API int spectra_p2p_allgather(const void* src, void* const* peer_buffers, int64_t buffer_bytes, void* out,
+                                      int64_t out_row_stride, int64_t M, int64_t ns, int64_t N, int64_t elem_bytes,
+                                      int* state, int rank, int world, int64_t wait_limit_ns, void* stream);
 
 /*
  * Diagnostic, not a reference interface (the reference's Triton kernels have

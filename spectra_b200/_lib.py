@@ -17,6 +17,8 @@ LAYOUT_EVEN_ODD, LAYOUT_MARLIN = 0, 1
 OK = 0
 ERR_NULL_POINTER, ERR_SHAPE, ERR_STRIDE, ERR_ALIGNMENT, ERR_DTYPE, ERR_WORKSPACE, ERR_CUDA, ERR_UNSUPPORTED = range(1, 9)
 ABI_VERSION = 1
+P2P_STATE_INTS = 128  # SPECTRA_P2P_STATE_INTS
+P2P_SIGNAL_BYTES = 8 * 128 * 4  # epoch flags [rank][cta] at the start of an exchange buffer
 
 # name -> (restype, argtypes)
 PROTOTYPES = {
@@ -75,6 +77,13 @@ PROTOTYPES = {
         c_int64, c_int64, c_int, c_void_p]),           # V, K, layout, stream
     "spectra_argmax": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "spectra_fwht": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_int64, c_int64, c_int64, c_int, c_void_p]),
+    "spectra_p2p_buffer_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int]),
+    "spectra_p2p_alloc": (c_int, [c_int64, c_void_p, c_void_p]),
+    "spectra_p2p_open": (c_int, [c_void_p, c_void_p]),
+    "spectra_p2p_close": (c_int, [c_void_p]),
+    "spectra_p2p_free": (c_int, [c_void_p]),
+    "spectra_p2p_allgather": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                      c_int64, c_void_p, c_int, c_int, c_int64, c_void_p]),
     "spectra_device_timeouts": (c_int, [c_void_p, c_int]),
     "spectra_selftest_wait_timeout": (c_int, [c_void_p]),
     "spectra_w4a16_dequant": (c_int, [

@@ -4,6 +4,7 @@
 #include <cuda.h>
 
 #include <cmath>
+#include <cstring>
 #include <cstdint>
 #include <cstdlib>
 
@@ -11,6 +12,7 @@
 #include "format.h"
 #include "gemm.h"
 #include "gemv.h"
+#include "p2p.h"
 
 namespace spectra {
 
@@ -237,13 +239,91 @@ int spectra_w4a16_gemm_noalloc(
 
 int spectra_device_timeouts(int64_t* count, int reset) {
   if (!count) return SPECTRA_ERR_NULL_POINTER;
-  long long a = 0, b = 0, c = 0;
+  long long a = 0, b = 0, c = 0, d = 0;
   int st = gemv_timeouts(&a, reset != 0);
   if (st == SPECTRA_OK) st = gemv_pf_timeouts(&b, reset != 0);
   if (st == SPECTRA_OK) st = gemm_timeouts(&c, reset != 0);
+  if (st == SPECTRA_OK) st = p2p_timeouts(&d, reset != 0);
   if (st != SPECTRA_OK) return st;
-  *count = int64_t(a + b + c);
+  *count = int64_t(a + b + c + d);
   return SPECTRA_OK;
+}
+
+int64_t spectra_p2p_buffer_bytes(int64_t M, int64_t ns, int64_t elem_bytes, int world) {
+  if (M < 1 || ns < 1 || world < 1 || world > kP2pMaxRanks || (elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8))
+    return -1;
+  if (M * ns * elem_bytes > (int64_t(1) << 34)) return -1;
+  return p2p_buffer_bytes(int(M), int(ns), int(elem_bytes), world);
+}
+
+int spectra_p2p_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle) return SPECTRA_ERR_NULL_POINTER;
+  if (bytes <= 0) return SPECTRA_ERR_SHAPE;
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, size_t(bytes));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, size_t(bytes));  // epoch slots start at 0
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();           // ... before any peer can see the handle
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return cuda_status(e);
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return SPECTRA_OK;
+}
+
+int spectra_p2p_open(const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return SPECTRA_ERR_NULL_POINTER;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int spectra_p2p_close(void* ptr) {
+  if (!ptr) return SPECTRA_ERR_NULL_POINTER;
+  return cuda_status(cudaIpcCloseMemHandle(ptr));
+}
+
+int spectra_p2p_free(void* ptr) {
+  if (!ptr) return SPECTRA_ERR_NULL_POINTER;
+  return cuda_status(cudaFree(ptr));
+}
+
+int spectra_p2p_allgather(const void* src, void* const* peer_buffers, int64_t buffer_bytes, void* out,
+                          int64_t out_row_stride, int64_t M, int64_t ns, int64_t N, int64_t elem_bytes, int* state,
+                          int rank, int world, int64_t wait_limit_ns, void* stream) {
+  if (!src || !peer_buffers || !out || !state) return SPECTRA_ERR_NULL_POINTER;
+  if (world < 1 || world > kP2pMaxRanks || rank < 0 || rank >= world) return SPECTRA_ERR_SHAPE;
+  if (M < 1 || ns < 1 || N < 1 || N > ns * world || wait_limit_ns <= 0)
+    return SPECTRA_ERR_SHAPE;
+  const int64_t need = spectra_p2p_buffer_bytes(M, ns, elem_bytes, world);
+  if (need < 0) return elem_bytes == 2 || elem_bytes == 4 || elem_bytes == 8 ? SPECTRA_ERR_SHAPE : SPECTRA_ERR_DTYPE;
+  if (buffer_bytes < need) return SPECTRA_ERR_WORKSPACE;
+  if (out_row_stride < N || M * out_row_stride > (int64_t(1) << 34)) return SPECTRA_ERR_STRIDE;
+  P2pArgs a{};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_buffers[r]) return SPECTRA_ERR_NULL_POINTER;
+    if (!aligned(peer_buffers[r], 16)) return SPECTRA_ERR_ALIGNMENT;
+    a.peer[r] = static_cast<uint8_t*>(peer_buffers[r]);
+  }
+  if (!aligned(src, 16) || !aligned(out, size_t(elem_bytes)) || !aligned(state, 4)) return SPECTRA_ERR_ALIGNMENT;
+  a.src = static_cast<const uint8_t*>(src);
+  a.out = static_cast<uint8_t*>(out);
+  a.out_rs = out_row_stride;
+  a.slice_pitch = p2p_slice_pitch(int(M), int(ns), int(elem_bytes));
+  a.state = state;
+  a.M = int(M);
+  a.ns = int(ns);
+  a.N = int(N);
+  a.elem_bytes = int(elem_bytes);
+  a.rank = rank;
+  a.world = world;
+  a.wait_limit_ns = uint64_t(wait_limit_ns);
+  return launch_p2p_allgather(a, static_cast<cudaStream_t>(stream));
 }
 
 int spectra_selftest_wait_timeout(void* stream) { return launch_selftest_wait(static_cast<cudaStream_t>(stream)); }

@@ -13,19 +13,23 @@
 // Argmax: the greedy next-token choice over logits [M, N] (the engine's
 // sample_token at temperature 0, spectra/engine.py:1690-1713, is
 // torch.argmax): first index of the maximum, a NaN counts as the maximum (as
-// in torch).  One CTA per row; `idx_offset` turns a shard's local index into
+// in torch).  One cluster of 8 CTAs per row; `idx_offset` turns a shard's local index into
 // the layer's row index, so the N-sharded lm_head reduces (value, index)
 // pairs across ranks instead of gathering every logit.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "format.h"
 #include "gemv_mma.cuh"
+#include "sm100_ptx.cuh"
 
 namespace spectra {
 
 namespace {
 
 constexpr int kEmbedThreads = 256;
-constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxCluster = 8;  // CTAs per row (a portable cluster size)
 
 __global__ void __launch_bounds__(kEmbedThreads) embedding_kernel(EmbedArgs a) {
   const int64_t t = blockIdx.x;
@@ -79,15 +83,54 @@ __device__ __forceinline__ bool better(float v, int64_t i, float bv, int64_t bi)
   return v > bv || (v == bv && i < bi);
 }
 
+// One row per cluster of kArgmaxCluster CTAs: CTA c scans the c-th slice of
+// the row with 16-byte loads where the row allows them, reduces it to one
+// (value, index) pair, and CTA 0 combines the cluster's pairs from the other
+// CTAs' shared memory (distributed shared memory; the cluster barriers are
+// hardware barriers over co-scheduled CTAs, nothing spins).
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(ArgmaxArgs a) {
-  const int64_t m = blockIdx.x;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  sm100::pdl_wait();  // the logits are the previous kernel's output
+  const int64_t m = blockIdx.y;
+  const int c = int(cluster.block_rank());
+  const int64_t lo = min(a.N, c * a.span), hi = min(a.N, lo + a.span);
   float bv = -INFINITY;
   int64_t bi = INT64_MAX;
-  for (int64_t n = threadIdx.x; n < a.N; n += blockDim.x) {
-    const float v = load_as_float_cg(a.x, m * a.x_rs + n, a.x_dtype);
-    if (better(v, n, bv, bi)) {
-      bv = v;
-      bi = n;
+  if (a.vec) {
+    // 16-byte units of the row (the row start is 16-byte aligned, the span a multiple of the unit)
+    const int per = a.x_dtype == SPECTRA_DT_F32 ? 4 : 8;
+    const uint4* row = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) +
+                                                      m * a.x_rs * (a.x_dtype == SPECTRA_DT_F32 ? 4 : 2));
+    const int64_t u_lo = lo / per, u_hi = (hi + per - 1) / per;
+    for (int64_t u = u_lo + threadIdx.x; u < u_hi; u += kArgmaxThreads) {
+      const uint4 w = __ldcg(row + u);
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e >= per) break;
+        const int64_t n = u * per + e;
+        if (n >= hi) break;
+        float v;
+        if (a.x_dtype == SPECTRA_DT_F32) {
+          v = __uint_as_float(wv[e]);
+        } else {
+          const uint32_t h = (wv[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+          v = a.x_dtype == SPECTRA_DT_BF16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(uint16_t(h)));
+        }
+        if (better(v, n, bv, bi)) {
+          bv = v;
+          bi = n;
+        }
+      }
+    }
+  } else {
+    for (int64_t n = lo + threadIdx.x; n < hi; n += kArgmaxThreads) {
+      const float v = load_as_float_cg(a.x, m * a.x_rs + n, a.x_dtype);
+      if (better(v, n, bv, bi)) {
+        bv = v;
+        bi = n;
+      }
     }
   }
 #pragma unroll
@@ -108,9 +151,32 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(ArgmaxArgs a) {
   }
   __syncthreads();
   if (warp == 0) {
-    const int nw = blockDim.x / 32;
+    constexpr int nw = kArgmaxThreads / 32;
     bv = lane < nw ? sv[lane] : -INFINITY;
     bi = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+  }
+  __syncthreads();  // every warp has read sv / si
+  if (threadIdx.x == 0) {
+    sv[0] = bv;  // this CTA's pair, for CTA 0 of the cluster
+    si[0] = bi;
+  }
+  cluster.sync();
+  if (c == 0 && warp == 0) {
+    bv = -INFINITY;
+    bi = INT64_MAX;
+    if (lane < kArgmaxCluster) {
+      bv = *cluster.map_shared_rank(&sv[0], lane);
+      bi = *cluster.map_shared_rank(&si[0], lane);
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -125,6 +191,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(ArgmaxArgs a) {
       if (a.val) a.val[m] = bv;
     }
   }
+  cluster.sync();  // no CTA leaves while CTA 0 may still read its shared memory
 }
 
 }  // namespace
@@ -136,11 +203,29 @@ int launch_embedding(const EmbedArgs& a, cudaStream_t st) {
   return cuda_status(cudaGetLastError());
 }
 
-int launch_argmax(const ArgmaxArgs& a, cudaStream_t st) {
+int launch_argmax(ArgmaxArgs a, cudaStream_t st) {
   if (a.M == 0) return SPECTRA_OK;
-  if (a.M > int64_t(INT32_MAX)) return SPECTRA_ERR_SHAPE;
-  argmax_kernel<<<unsigned(a.M), kArgmaxThreads, 0, st>>>(a);
-  return cuda_status(cudaGetLastError());
+  if (a.M > 65535) return SPECTRA_ERR_SHAPE;  // grid y
+  // 16-byte loads when every row starts on a 16-byte boundary and each CTA's
+  // slice is a whole number of 16-byte units
+  const int64_t esz = a.x_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  const int64_t per = 16 / esz;
+  a.span = ((a.N + kArgmaxCluster - 1) / kArgmaxCluster + per - 1) / per * per;  // whole 16-byte units
+  a.vec = reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.M == 1 || (a.x_rs * esz) % 16 == 0);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kArgmaxCluster, unsigned(a.M));
+  cfg.blockDim = dim3(kArgmaxThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kArgmaxCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, argmax_kernel, a));
 }
 
 }  // namespace spectra

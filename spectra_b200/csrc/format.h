@@ -58,8 +58,10 @@ struct ArgmaxArgs {
   int64_t* idx;                              // [M]
   float* val;                                // [M] or NULL
   int64_t M; int64_t N; int64_t idx_offset;  // idx_offset added to every index (a shard's first row)
+  int64_t span;                              // elements per CTA of a row's cluster (set by the launcher)
+  bool vec;                                  // 16-byte loads (set by the launcher)
 };
-int launch_argmax(const ArgmaxArgs& a, cudaStream_t st);
+int launch_argmax(ArgmaxArgs a, cudaStream_t st);
 
 // Walsh-Hadamard rotation of activation rows (fwht.cu).
 struct FwhtArgs {

@@ -8,11 +8,16 @@ with the same kernels as the unsharded layer (the M=1 GEMV with bias fused,
 else the tensor-core GEMM plus bias, exactly as ``SpectraFusedLinear.forward``
 routes them, spectra/engine.py:90-124), writing straight into a persistent
 [M, Ns] buffer of this rank (rows past N stay zero: a ragged last shard costs
-no extra kernel), then one all-gather over the process group assembles
-[M, N].  This is the only collective: the slices are independent.
+no extra kernel), then one all-gather assembles [M, N].  This is the only
+collective: the slices are independent.
 
-The gathered buffer is laid out [g, M, Ns]; for M = 1 it already is the output
-row (no copy), for M > 1 one transpose copy makes it [M, N].
+The all-gather, on GPUs of one node, is this package's peer-memory exchange
+(spectra_b200.p2p: one kernel pushes the slice into every peer's buffer over
+NVLink, flags it, and writes the gathered [M, N] output), with the slice
+buffer being the exchange's source, so a call is two kernels; elsewhere (gloo,
+or ``exchange="collective"``, or SPECTRA_B200_P2P=0 in the environment) it is
+the process group's ``all_gather_into_tensor`` into a [g, M, Ns] buffer, which
+for M = 1 already is the output row and for M > 1 takes one transpose copy.
 
 Greedy decode does not need the whole row of logits on every rank:
 ``greedy(x)`` computes this rank's slice, its first maximum with the argmax
@@ -28,6 +33,7 @@ gather latency is counted, so callers shard only large layers.
 """
 from __future__ import annotations
 
+import os
 from typing import Callable, Dict, Optional, Tuple
 
 import torch
@@ -74,13 +80,23 @@ class ShardedW4A16Linear:
     out)`` writes one rank's slice into ``out``; it defaults to the CUDA kernels
     (tests on CPU pass a reference implementation instead), as does
     ``argmax_fn(y, offset) -> (values, indices)``.
+
+    ``exchange``: "auto" (the peer-memory exchange when the group's backend is
+    NCCL on CUDA devices and SPECTRA_B200_P2P is not 0, else the group's
+    all-gather), "p2p" or "collective".  ``wait_limit_s`` bounds the
+    exchange kernel's wait for a peer.  The first call of each M is collective
+    (it sets up that shape's exchange buffers on every rank); ``close()``
+    releases them, collectively.
     """
 
     def __init__(self, packed: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                  outlier_idx: Optional[torch.Tensor] = None, outlier_w: Optional[torch.Tensor] = None,
                  bias: Optional[torch.Tensor] = None, marlin_layout: bool = False,
                  group: Optional[dist.ProcessGroup] = None, device: Optional[torch.device] = None,
-                 local_fn: Optional[Callable] = None, argmax_fn: Optional[Callable] = None):
+                 local_fn: Optional[Callable] = None, argmax_fn: Optional[Callable] = None,
+                 exchange: str = "auto", wait_limit_s: float = 5.0):
+        if exchange not in ("auto", "p2p", "collective"):
+            raise ValueError(f"exchange must be 'auto', 'p2p' or 'collective', not {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -102,16 +118,49 @@ class ShardedW4A16Linear:
         self.local_fn = local_fn or _kernel_local
         self.argmax_fn = argmax_fn or _kernel_argmax
         self._local_bufs: Dict[Tuple[int, torch.dtype], torch.Tensor] = {}
+        self._exchanges: Dict[tuple, object] = {}
+        self.wait_limit_s = wait_limit_s
+        self.use_p2p = False
+        if self.world > 1 and exchange != "collective":
+            on_nccl = torch.device(dev).type == "cuda" and "nccl" in str(dist.get_backend(group))
+            wanted = exchange == "p2p" or os.environ.get("SPECTRA_B200_P2P", "1") != "0"
+            if exchange == "p2p" and not on_nccl:
+                raise ValueError("the peer-memory exchange needs an NCCL group on CUDA devices")
+            self.use_p2p = on_nccl and wanted
+
+    def _exchange(self, key: tuple, M: int, ns: int, N: int, dtype: torch.dtype):
+        """The peer-memory exchange of one gathered shape, set up on first use
+        (collectively); None (on every rank alike) when setup failed and
+        exchange is "auto", in which case the group's all-gather is used."""
+        if key not in self._exchanges:
+            from .p2p import PeerExchange
+            try:
+                self._exchanges[key] = PeerExchange(M, ns, N, dtype, self.device, self.group, self.wait_limit_s)
+            except RuntimeError:
+                self._exchanges[key] = None
+        return self._exchanges[key]
 
     def _local_buffer(self, M: int, dtype: torch.dtype) -> torch.Tensor:
-        """Persistent [M, Ns] slice buffer: zero-filled once, so the rows past the
+        """Persistent [M, Ns] slice buffer (the exchange's source when the
+        peer-memory exchange is on): zero-filled once, so the rows past the
         layer's end (ragged last shard) stay zero without a kernel per call."""
+        if self.use_p2p:
+            ex = self._exchange(("y", M, dtype), M, self.ns, self.N, dtype)
+            if ex is not None:
+                return ex.src
         key = (M, dtype)
         buf = self._local_bufs.get(key)
         if buf is None:
             buf = torch.zeros(M, self.ns, dtype=dtype, device=self.device)
             self._local_bufs[key] = buf
         return buf
+
+    def close(self) -> None:
+        """Releases the exchange buffers (collective: every rank calls it)."""
+        for ex in self._exchanges.values():
+            if ex is not None:
+                ex.close()
+        self._exchanges = {}
 
     def local(self, x2d: torch.Tensor) -> torch.Tensor:
         """[M, Ns] slice of this rank (rows past the layer's end are zero)."""
@@ -128,8 +177,11 @@ class ShardedW4A16Linear:
         M = x.numel() // self.in_features
         x2d = x.reshape(M, self.in_features)
         y_local = self.local(x2d)
+        ex = self._exchanges.get(("y", M, y_local.dtype)) if self.use_p2p else None
         if self.world == 1:
             y = y_local[:, :self.N]
+        elif ex is not None:
+            y = ex.gather()
         else:
             gathered = torch.empty(self.world * M * self.ns, device=y_local.device, dtype=y_local.dtype)
             dist.all_gather_into_tensor(gathered, y_local.reshape(-1), group=self.group)
@@ -149,17 +201,24 @@ class ShardedW4A16Linear:
         M = x.numel() // self.in_features
         x2d = x.reshape(M, self.in_features)
         y_local = self.local(x2d)
+        ex = None
+        if self.use_p2p:
+            ex = self._exchange(("pair", M), M, 2, 2 * self.world, torch.float64)
+        pair = ex.src if ex is not None else torch.empty(M, 2, dtype=torch.float64, device=y_local.device)
         if self.rows > 0:
             val, idx = self.argmax_fn(y_local[:, :self.rows], self.row0)
-            pair = torch.stack([val.to(torch.float64), idx.to(torch.float64)], dim=1)  # [M, 2], exact
+            torch.stack([val.to(torch.float64), idx.to(torch.float64)], dim=1, out=pair)  # [M, 2], exact
         else:  # an empty shard never wins
-            pair = torch.tensor([[float("-inf"), float(2 ** 53)]], dtype=torch.float64,
-                                device=y_local.device).expand(M, 2).contiguous()
+            pair[:, 0] = float("-inf")
+            pair[:, 1] = float(2 ** 53)
         if self.world == 1:
             return pair[:, 1].to(torch.int64).reshape(orig_shape[:-1])
-        gathered = torch.empty(self.world * M * 2, dtype=torch.float64, device=pair.device)
-        dist.all_gather_into_tensor(gathered, pair.reshape(-1), group=self.group)
-        g = gathered.view(self.world, M, 2)
+        if ex is not None:
+            g = ex.gather().view(M, self.world, 2).transpose(0, 1)
+        else:
+            gathered = torch.empty(self.world * M * 2, dtype=torch.float64, device=pair.device)
+            dist.all_gather_into_tensor(gathered, pair.reshape(-1), group=self.group)
+            g = gathered.view(self.world, M, 2)
         # ranks hold increasing row ranges: the first maximum in rank order is the
         # first maximum of the row (torch.argmax: the first NaN counts as maximum)
         r = torch.argmax(g[:, :, 0], dim=0)

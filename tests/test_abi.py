@@ -44,6 +44,7 @@ def test_header_constants_match_binding():
     assert int(consts["SPECTRA_LAYOUT_MARLIN"]) == L.LAYOUT_MARLIN
     assert int(consts["SPECTRA_ERR_CUDA"]) == L.ERR_CUDA
     assert int(consts["SPECTRA_ERR_UNSUPPORTED"]) == L.ERR_UNSUPPORTED
+    assert int(consts["SPECTRA_P2P_STATE_INTS"]) == L.P2P_STATE_INTS
 
 
 # Fake, never-dereferenced device addresses: every call below fails its host

@@ -108,7 +108,7 @@ CONFIG3 = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096)]
 def test_config3_gemm_and_gemv(K, N):
     rows = sample_rows(N, 192, seed=K + N)
     c = compress_and_pin(N, K, seed=K * 7 + N, dist="n002", rows=rows)
-    for M in (16, 64, 256):
+    for M in (2, 4, 8, 16, 64, 256):  # 2 and 4: the engine's generate_batch; 16-256: config 3
         a = act(M, K, seed=M * 13 + K)
         out = SK.batched_w4a16_gemm(a, c.packed, c.scales, c.zeros, outlier_idx=c.outlier_idx,
                                     outlier_w=c.outlier_w, marlin_layout=True)

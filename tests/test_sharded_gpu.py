@@ -2,7 +2,10 @@
 rows with the CUDA kernels, must assemble the full layer's output -- the same
 on every rank and within the GEMV / GEMM parity bars of the oracle's result
 (M = 1 and M = 32, ragged last shard, outliers, bias); the sharded greedy
-head picks the first maximum of that output.  Needs >= 2 GPUs."""
+head picks the first maximum of that output.  Both exchanges are run: the
+peer-memory all-gather over NVLink (the default on NCCL groups) and the
+group's own all-gather, and must agree bit for bit; the peer-memory path is
+also captured in a CUDA graph and replayed on fresh inputs.  Needs >= 2 GPUs."""
 import os
 import socket
 
@@ -35,27 +38,67 @@ def _layer(N, K, n_out, seed):
     return f, bias
 
 
+def _x(M, K, seed):
+    return torch.randn(M, K, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+
+
 def _worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    layers = []
     try:
+        from spectra_b200 import kernels as SK
         from spectra_b200.sharded import ShardedW4A16Linear
+        SK.device_timeouts(reset=True)
         out = []
         for N, K, n_out, M, seed in CASES:
             f, bias = _layer(N, K, n_out, seed)
-            lin = ShardedW4A16Linear(torch.from_numpy(f["packed"]), torch.from_numpy(f["scales"]),
-                                     torch.from_numpy(f["zeros"]), outlier_idx=torch.from_numpy(f["outlier_idx"]),
-                                     outlier_w=f["outlier_w_t"], bias=bias, marlin_layout=True,
-                                     device=torch.device("cuda", rank))
-            x = torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 7)).to(torch.bfloat16)
-            y = lin.forward(x.cuda(rank))
-            tok = lin.greedy(x.cuda(rank))
-            torch.cuda.synchronize()
-            out.append((y.float().cpu().numpy(), tok.cpu().numpy()))
+            res = {}
+            for exchange in ("p2p", "collective"):
+                lin = ShardedW4A16Linear(torch.from_numpy(f["packed"]), torch.from_numpy(f["scales"]),
+                                         torch.from_numpy(f["zeros"]),
+                                         outlier_idx=torch.from_numpy(f["outlier_idx"]), outlier_w=f["outlier_w_t"],
+                                         bias=bias, marlin_layout=True, device=dev, exchange=exchange)
+                layers.append(lin)
+                assert lin.use_p2p == (exchange == "p2p")
+                x = _x(M, K, seed + 7).to(dev)
+                y = lin.forward(x)
+                y2 = lin.forward(x)   # second call: the other buffer parity
+                tok = lin.greedy(x)
+                torch.cuda.synchronize()
+                assert torch.equal(y, y2)
+                res[exchange] = (y.float().cpu().numpy(), tok.cpu().numpy())
+                if exchange == "p2p":
+                    assert lin._exchanges[("y", M, torch.bfloat16)] is not None
+                    # graph capture of the two-kernel call, replayed on new inputs
+                    xs = x.clone()
+                    lin.forward(xs), lin.greedy(xs)  # warm-up on the capture's shapes
+                    torch.cuda.synchronize()
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        yg = lin.forward(xs)
+                        tg = lin.greedy(xs)
+                    reps = []
+                    for j in range(3):
+                        xj = _x(M, K, 1000 * seed + j).to(dev)
+                        xs.copy_(xj)
+                        g.replay()
+                        torch.cuda.synchronize()
+                        reps.append((yg.clone(), tg.clone(), lin.forward(xj), lin.greedy(xj)))
+                    for yr, tr, ye, te in reps:
+                        assert torch.equal(yr, ye) and torch.equal(tr, te), "graph replay differs from eager"
+                    del g
+            out.append((res["p2p"], res["collective"]))
+        torch.cuda.synchronize()
+        out.append(SK.device_timeouts())
         q.put((rank, out))
     finally:
+        for lin in layers:
+            lin.close()
         dist.destroy_process_group()
 
 
@@ -73,13 +116,18 @@ def test_sharded_layer_on_two_gpus_matches_oracle():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    assert res[0][-1] == 0 and res[1][-1] == 0, "a device wait timed out"
     for i, (N, K, n_out, M, seed) in enumerate(CASES):
-        (y0, t0), (y1, t1) = res[0][i], res[1][i]
+        (y0, t0), (yc0, tc0) = res[0][i]
+        (y1, t1), (yc1, tc1) = res[1][i]
         assert np.array_equal(y0, y1), f"ranks disagree on case {i}"
+        # the peer-memory exchange and the group's all-gather assemble the same bits
+        assert np.array_equal(y0, yc0) and np.array_equal(y1, yc1), f"exchanges differ, case {i}"
+        assert np.array_equal(t0, tc0) and np.array_equal(t1, tc1)
         # the (value, index) reduction picks the first maximum of the gathered row
         assert np.array_equal(t0, t1) and np.array_equal(t0, np.argmax(y0, axis=-1)), f"greedy, case {i}"
         f, bias = _layer(N, K, n_out, seed)
-        x = torch.randn(M, K, generator=torch.Generator().manual_seed(seed + 7)).to(torch.bfloat16)
+        x = _x(M, K, seed + 7)
         ow, owd = np_of(f["outlier_w_t"])
         bn, bd = np_of(bias)
         for m in range(M):
