@@ -212,6 +212,10 @@ int spectra_w4a16_gemm(
   g.ow = has_out ? outlier_w : nullptr; g.ow_dtype = ow_dtype; g.ow_rs = ow_row_stride; g.ow_cs = ow_col_stride;
   g.c = c; g.c_dtype = c_dtype; g.c_rs = c_row_stride;
   g.M = int(M); g.N = int(N); g.K = int(K); g.layout = layout;
+  if (M <= 8) {  // decode batch sizes: the raw-code small-M kernel when its layout conditions hold
+    const int r = launch_gemv_mt(g, static_cast<cudaStream_t>(stream));
+    if (r != SPECTRA_ERR_UNSUPPORTED) return r;
+  }
   return launch_gemm(g, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -239,13 +243,14 @@ int spectra_w4a16_gemm_noalloc(
 
 int spectra_device_timeouts(int64_t* count, int reset) {
   if (!count) return SPECTRA_ERR_NULL_POINTER;
-  long long a = 0, b = 0, c = 0, d = 0;
+  long long a = 0, b = 0, c = 0, d = 0, e = 0;
   int st = gemv_timeouts(&a, reset != 0);
   if (st == SPECTRA_OK) st = gemv_pf_timeouts(&b, reset != 0);
   if (st == SPECTRA_OK) st = gemm_timeouts(&c, reset != 0);
   if (st == SPECTRA_OK) st = p2p_timeouts(&d, reset != 0);
+  if (st == SPECTRA_OK) st = gemv_mt_timeouts(&e, reset != 0);
   if (st != SPECTRA_OK) return st;
-  *count = int64_t(a + b + c + d);
+  *count = int64_t(a + b + c + d + e);
   return SPECTRA_OK;
 }
 

@@ -73,3 +73,52 @@ def assert_close_to_oracle(y_gpu: np.ndarray, y_exact: np.ndarray, y_round: np.n
 
 def act(M: int, K: int, seed: int, dtype: str) -> torch.Tensor:
     return draw_act(M, K, seed=seed, dtype=TORCH_DT[dtype])
+
+
+_DT_CODE = {"f16": 0, "bf16": 1, "f32": 2}
+
+
+def small_m_path(M: int, N: int, K: int, n_out: int, a_dtype: str = "bf16", ow_dtype: str = "bf16") -> bool:
+    """Whether spectra_w4a16_gemm runs its small-M kernel (M = 2..8, exact
+    dequantised weights) for contiguous operands of this shape on GPU 0."""
+    import ctypes
+    from spectra_b200 import _lib as L
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    out = np.zeros(5, np.int64)
+    cd = "bf16" if a_dtype == "bf16" else "f16"
+    st = L.lib().spectra_gemm_small_m_plan(M, N, K, n_out, _DT_CODE[cd], _DT_CODE[ow_dtype], sms,
+                                          out.ctypes.data_as(ctypes.c_void_p))
+    return st == 0 and out[0] == 1
+
+
+def gemm_exact_weights(a, a_dtype: str, packed, scales, zeros, outlier_idx=None, outlier_w=None,
+                       ow_dtype=None, marlin: bool = True):
+    """The small-M kernel's semantics: activations rounded to the compute dtype
+    (as the reference GEMM's operands), the dequantised weights and outlier
+    weights exact (as the reference GEMV), exact accumulation, one rounding.
+    Returns (c_exact, c_rounded, compute_dtype)."""
+    cd = "bf16" if a_dtype == "bf16" else "f16"
+    av = O.round_to(O._as_f64(a, a_dtype), cd)
+    av = av.reshape(-1, av.shape[-1])
+    w = O.dequant_f32(packed, scales, zeros, marlin).astype(np.float64)
+    c = av @ w.T
+    if outlier_idx is not None and outlier_w is not None and np.asarray(outlier_idx).size:
+        idx = np.asarray(outlier_idx, np.int64)
+        c = c + av[:, idx] @ O._as_f64(outlier_w, ow_dtype).T
+    return c, O.round_to(c, cd), cd
+
+
+def operand_rounding_bound(a, a_dtype: str, packed, scales, zeros, outlier_idx=None, outlier_w=None,
+                           ow_dtype=None, marlin: bool = True) -> np.ndarray:
+    """Per output, sum_k |a_k| |w_k - R(w_k)| (+ the same over the outlier
+    columns): how far the reference GEMM's operand rounding R() can move a
+    result away from the exact-weights product."""
+    cd = "bf16" if a_dtype == "bf16" else "f16"
+    av = np.abs(O.round_to(O._as_f64(a, a_dtype), cd)).reshape(-1, np.asarray(packed).shape[1] * 2)
+    w = O.dequant_f32(packed, scales, zeros, marlin).astype(np.float64)
+    e = av @ np.abs(w - O.round_to(w, cd)).T
+    if outlier_idx is not None and outlier_w is not None and np.asarray(outlier_idx).size:
+        idx = np.asarray(outlier_idx, np.int64)
+        ow = O._as_f64(outlier_w, ow_dtype)
+        e = e + av[:, idx] @ np.abs(ow - O.round_to(ow, cd)).T
+    return e

@@ -21,7 +21,7 @@ import torch
 from oracle import w4a16 as O
 from spectra_b200 import compress as C
 from spectra_b200 import kernels as SK
-from tests.helpers import assert_close_to_oracle, np_of, out_f64
+from tests.helpers import assert_close_to_oracle, gemm_exact_weights, np_of, out_f64, small_m_path
 
 pytestmark = pytest.mark.gpu
 
@@ -74,13 +74,21 @@ def rows_fmt(c, rows: np.ndarray) -> dict:
 
 
 def check_gemm_rows(c, a: torch.Tensor, out: torch.Tensor, rows: np.ndarray, what: str):
+    """The GEMM's bar on the sampled rows: against the reference's operand
+    rounding for the tcgen05 kernel; against the exact dequantised weights
+    (1 ulp) and the operand rounding (1e-2*||c||_inf) when the small-M kernel
+    (M = 2..8) took the call."""
     f = rows_fmt(c, rows)
     an, ad = np_of(a)
     ow, owd = np_of(f["ow"])
-    c_exact, c_round, cd = O.gemm(an, ad, f["packed"], f["scales"], f["zeros"], outlier_idx=f["outlier_idx"],
-                                  outlier_w=ow, ow_dtype=owd, marlin=True)
+    kw = dict(outlier_idx=f["outlier_idx"], outlier_w=ow, ow_dtype=owd, marlin=True)
+    c_exact, c_round, cd = O.gemm(an, ad, f["packed"], f["scales"], f["zeros"], **kw)
     got = out_f64(out[:, torch.from_numpy(rows).to(DEV)])
     assert np.isfinite(got).all(), what
+    M, K = a.shape
+    if small_m_path(M, int(c.packed.shape[0]), K, int(c.outlier_idx.numel()), ad, owd):
+        assert np.max(np.abs(got - c_exact)) <= 1e-2 * np.max(np.abs(c_exact)), what
+        c_exact, c_round, cd = gemm_exact_weights(an, ad, f["packed"], f["scales"], f["zeros"], **kw)
     assert_close_to_oracle(got, c_exact, c_round, cd, what)
 
 

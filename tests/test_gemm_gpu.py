@@ -1,7 +1,11 @@
-"""GPU parity of the M >= 2 tensor-core GEMM (batched_w4a16_gemm) against the
-reference's own outputs and the oracle.  Bar: within 1e-2*||c||_inf of the
-exact result of the reference's operand rounding, and within 1 output ulp of
-its correctly rounded value (floor 2^-16*||c||_inf)."""
+"""GPU parity of the M >= 2 GEMM (batched_w4a16_gemm) against the reference's
+own outputs and the oracle.  Bar for the tcgen05 kernel: within 1e-2*||c||_inf
+of the exact result of the reference's operand rounding, and within 1 output
+ulp of its correctly rounded value (floor 2^-16*||c||_inf).  Calls the small-M
+kernel takes (M = 2..8, spectra_gemm_small_m_plan) use the exact dequantised
+weights instead: the same 1-ulp bar against that exact result, 1e-2*||c||_inf
+against the operand-rounded one, and against the reference's own outputs one
+output ulp each side plus the most the operand rounding can move a result."""
 import numpy as np
 import pytest
 import torch
@@ -9,7 +13,8 @@ import torch
 from oracle import w4a16 as O
 from spectra_b200 import _lib as L
 from spectra_b200 import kernels as SK
-from tests.helpers import TORCH_DT, act, assert_close_to_oracle, compressed, np_of, out_f64, random_format, ulp
+from tests.helpers import (TORCH_DT, act, assert_close_to_oracle, compressed, gemm_exact_weights, np_of, out_f64,
+                           operand_rounding_bound, random_format, small_m_path, ulp)
 
 pytestmark = pytest.mark.gpu
 
@@ -38,6 +43,22 @@ def oracle_gemm(fmt, a, marlin=True, use_out=True):
                   ow_dtype=owd, marlin=marlin)
 
 
+def takes_small_m(fmt, a, use_out=True):
+    N, K = fmt["packed"].shape[0], fmt["packed"].shape[1] * 2
+    n_out = int(fmt["outlier_idx"].size) if use_out else 0
+    _, owd = np_of(fmt["outlier_w_t"])
+    return small_m_path(a.numel() // K, N, K, n_out, np_of(a)[1], owd)
+
+
+def oracle_exact_weights(fmt, a, marlin=True, use_out=True):
+    an, ad = np_of(a.reshape(-1, a.shape[-1]))
+    ow, owd = np_of(fmt["outlier_w_t"])
+    has = use_out and fmt["outlier_idx"].size
+    return gemm_exact_weights(an, ad, fmt["packed"], fmt["scales"], fmt["zeros"],
+                              outlier_idx=fmt["outlier_idx"] if has else None, outlier_w=ow if has else None,
+                              ow_dtype=owd, marlin=marlin)
+
+
 def check(fmt, a, marlin=True, use_out=True, what=""):
     c = run_gemm(fmt, a, marlin, use_out)
     c_exact, c_round, cd = oracle_gemm(fmt, a, marlin, use_out)
@@ -45,6 +66,9 @@ def check(fmt, a, marlin=True, use_out=True, what=""):
     assert c.shape == a.shape[:-1] + (fmt["packed"].shape[0],)
     got = out_f64(c).reshape(c_exact.shape)
     assert np.isfinite(got).all(), what
+    if takes_small_m(fmt, a, use_out):
+        assert np.max(np.abs(got - c_exact)) <= 1e-2 * np.max(np.abs(c_exact)), what
+        c_exact, c_round, cd = oracle_exact_weights(fmt, a, marlin, use_out)
     assert_close_to_oracle(got, c_exact, c_round, cd, what)
     return c
 
@@ -84,14 +108,28 @@ def test_gemm_matches_reference_outputs(golden_dir, name, dt, marlin, use_out):
     # fp32 accumulation error where the sum cancels (the *_out fixtures pit
     # outlier terms against the main sum): floor 2^-16 * ||c||_inf.
     bound = np.maximum(ulp(c_ref, dt), np.exp2(-16.0) * np.max(np.abs(c_ref)))
+    small = M_of(a) > 1 and takes_small_m(fmt, a, use_out)
+    if small:
+        # exact dequantised weights here, rounded operands there: one ulp each
+        # side plus the most the operand rounding can move the result
+        an, ad = np_of(a.reshape(-1, a.shape[-1]))
+        ow_n, owd = np_of(fmt["outlier_w_t"])
+        e = operand_rounding_bound(an, ad, fmt["packed"], fmt["scales"], fmt["zeros"],
+                                   outlier_idx=fmt["outlier_idx"] if use_out else None,
+                                   outlier_w=ow_n if use_out else None, ow_dtype=owd, marlin=marlin)
+        bound = np.maximum(bound, 2 * ulp(c_ref, dt) + e.reshape(c_ref.shape) * 1.0001)
     d_rel = np.abs(got - c_ref) / bound
     i = np.unravel_index(int(np.argmax(d_rel)), d_rel.shape)
     assert d_rel[i] <= 1.0, (f"{name}: worst at {i}: got {got[i]!r} ref {c_ref[i]!r} "
                              f"({d_rel[i]:.2f} x max(1 ulp, 2^-16*||c||inf))")
     if dt == "f16":
         assert np.max(np.abs(got - c_ref)) <= 0.05  # tests/test_kernels.py:58
-    c_exact, c_round, cd = oracle_gemm(fmt, a, marlin, use_out)
+    c_exact, c_round, cd = (oracle_exact_weights if small else oracle_gemm)(fmt, a, marlin, use_out)
     assert_close_to_oracle(got, c_exact, c_round, cd, name)
+
+
+def M_of(a):
+    return a.numel() // a.shape[-1]
 
 
 # ---------------------------------------------------------------------------
