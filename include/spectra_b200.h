@@ -360,9 +360,9 @@ SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_out, int x_
  * Diagnostic, not a reference interface: whether spectra_w4a16_gemm takes its
  * small-M kernel for an [M, K] x [N, K] product with contiguous, 16-byte
  * aligned operands and n_out outlier columns of ow_dtype stored [N, n_out],
- * on a GPU with `sms` SMs (host only, no GPU).  out[5]: 1 if it does (else all
+ * on a GPU with `sms` SMs (host only, no GPU).  out[6]: 1 if it does (else all
  * zero: the tcgen05 GEMM runs), grid, dynamic shared memory bytes, ring
- * stages, outlier rows staged before the wait (1/0).  The kernel takes
+ * stages, outlier rows staged before the wait (1/0), compute groups.  The kernel takes
  * 2 <= M <= 8, K a multiple of 512, bf16/fp16 activations, when the staged
  * activations of all M rows and two weight stages fit in shared memory.
  * SPECTRA_B200_GEMM_SMALL_M=0 in the environment turns it off.

@@ -51,8 +51,7 @@ namespace spectra {
 
 namespace {
 
-constexpr int kMtWarps = 8;                  // compute warps: one 256-k unit each per stage
-constexpr int kMtThreads = (kMtWarps + 1) * 32;
+constexpr int kMtGroupWarps = 8;             // warps of a compute group: one 256-k unit each per stage
 constexpr int kMtMaxStages = 8;
 constexpr int kMtChunk = 2048;               // k per stage
 constexpr int kMtCodePitch = kMtChunk / 2 + 16;        // bytes per staged code row (130 x 8 B)
@@ -74,6 +73,7 @@ struct MtParams {
   int off_stage;
   int rows_max;
   int vec_a;                // 16-byte activation loads
+  int ng;                   // compute groups (alternate stages)
 };
 
 struct MtMaps {
@@ -120,12 +120,18 @@ __device__ __forceinline__ bool mt_wait(uint64_t* bar, uint32_t parity, const vo
   }
 }
 
-__device__ __forceinline__ void mt_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kMtWarps * 32) : "memory"); }
+template <int NT>
+__device__ __forceinline__ void mt_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
 
-template <bool BF16>
-__global__ void __launch_bounds__(kMtThreads, 1)
+// NG compute groups of 8 warps (group i takes stages i, i + NG, ...) and one
+// producer warp.
+template <bool BF16, int NG>
+__global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
     gemv_mt_kernel(const __grid_constant__ MtMaps maps, const __grid_constant__ MtParams kp) {
   using namespace sm100;
+  constexpr int kMtWarps = NG * kMtGroupWarps;  // compute warps
   const GemmArgs& p = kp.a;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kMtMaxStages];
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
     s_abort = 0;
     for (int s = 0; s < kp.ns; ++s) {
       mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kMtWarps);
+      mbar_init(&empty_bar[s], kMtGroupWarps);  // a stage is consumed by one group
     }
     mbar_init(&ow_bar, ow_staged ? 2 : 1);
     fence_mbar_init();
@@ -283,7 +289,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
   }
   for (int i = tid; i < G * kMtTok; i += kCT)
     if ((i & 7) >= M) xsum[i] = 0.f;
-  mt_bar();
+  mt_bar<kCT>();
 
   // ------------------------------------------------------------ main loop
   uint32_t magic_reg;
@@ -295,25 +301,34 @@ __global__ void __launch_bounds__(kMtThreads, 1)
   const int lm_row = (lane & 7) + 8 * ((lane >> 3) & 1);
   const int lm_grp = lane >> 4;
   const int KB = p.K >> 8;  // 256-feature units per row
-  int s = 0;
+  const int grp_id = NG == 1 ? 0 : warp / kMtGroupWarps;  // compute group, and warp inside it
+  const int w8 = NG == 1 ? warp : warp % kMtGroupWarps;
+  // Stages are consumed in issue order: stage si by group si % NG.  With two
+  // groups the ring depth is even, so a group's previous use of a ring slot
+  // was its own and was waited for.
+  int s = 0, si = 0;
   uint32_t ph = 0;
   for (int rb = 0; rb < nrb; ++rb) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int ch = 0; ch < kp.nkc; ++ch) {
+    for (int ch = 0; ch < kp.nkc; ++ch, ++si) {
+      if (NG > 1 && si % NG != grp_id) {
+        if (++s == kp.ns) { s = 0; ph ^= 1u; }
+        continue;
+      }
       bool ready = mt_wait(&full_bar[s], ph, &s_abort);
       ready = __all_sync(0xffffffffu, ready);
       if (!ready) {
         if (lane == 0) { s_abort = 1; atomicAdd(&g_gemv_mt_timeouts, 1); }
       } else {
-        const int kb = ch * (kMtChunk / 256) + warp;  // this warp's unit along K
+        const int kb = ch * (kMtChunk / 256) + w8;  // this warp's unit along K
         if (kb < KB) {
           const uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
-          const uint8_t* cst = st + warp * 128;  // the unit's first group: 8 groups x 16 B
+          const uint8_t* cst = st + w8 * 128;  // the unit's first group: 8 groups x 16 B
           // scales / zero points of the unit's 8 groups, rows g and g+8
-          const uint4 sa4 = *reinterpret_cast<const uint4*>(st + kp.off_sc + g * kMtScalePitch + warp * 16);
-          const uint4 sb4 = *reinterpret_cast<const uint4*>(st + kp.off_sc + (g + 8) * kMtScalePitch + warp * 16);
-          const uint2 za2 = *reinterpret_cast<const uint2*>(st + kp.off_z + g * kMtZeroPitch + warp * 8);
-          const uint2 zb2 = *reinterpret_cast<const uint2*>(st + kp.off_z + (g + 8) * kMtZeroPitch + warp * 8);
+          const uint4 sa4 = *reinterpret_cast<const uint4*>(st + kp.off_sc + g * kMtScalePitch + w8 * 16);
+          const uint4 sb4 = *reinterpret_cast<const uint4*>(st + kp.off_sc + (g + 8) * kMtScalePitch + w8 * 16);
+          const uint2 za2 = *reinterpret_cast<const uint2*>(st + kp.off_z + g * kMtZeroPitch + w8 * 8);
+          const uint2 zb2 = *reinterpret_cast<const uint2*>(st + kp.off_z + (g + 8) * kMtZeroPitch + w8 * 8);
           const uint32_t sa[4] = {sa4.x, sa4.y, sa4.z, sa4.w}, sb[4] = {sb4.x, sb4.y, sb4.z, sb4.w};
           const uint32_t za[2] = {za2.x, za2.y}, zb[2] = {zb2.x, zb2.y};
 #pragma unroll
@@ -363,7 +378,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
     ow_ok = __all_sync(0xffffffffu, ow_ok);
     if (!ow_ok && lane == 0) { s_abort = 1; atomicAdd(&g_gemv_mt_timeouts, 1); }
   }
-  mt_bar();
+  mt_bar<kCT>();
   // eight threads per row: outlier features j = sub, sub + 8, ... for all
   // tokens, then a transposing reduction leaves token reduced_row<8>(lane) of
   // the row in each thread
@@ -410,7 +425,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
     if (i < nrows && t < M) {
       float y = 0.f;
 #pragma unroll
-      for (int w8 = 0; w8 < kMtWarps; ++w8) y += red[(int64_t(w8) * rows_max + i) * kMtTok + t];
+      for (int ww = 0; ww < kMtWarps; ++ww) y += red[(int64_t(ww) * rows_max + i) * kMtTok + t];
       y += v[0];
       store_from_float(p.c, int64_t(t) * p.c_rs + r_begin + i, p.c_dtype, y);
     }
@@ -454,28 +469,39 @@ bool plan_gemv_mt(const GemmArgs& a, int sms, MtParams& kp, int64_t& grid, size_
   kp.off_xos = int(off);
   off = r16(off + size_t(a.n_out) * kMtTok * 4);
   kp.off_red = int(off);
-  off = r16(off + size_t(kMtWarps) * kp.rows_max * kMtTok * 4);
+  const size_t red_base = off;
+  const int64_t units = rb_max * kp.nkc;
   kp.off_sc = 16 * kMtCodePitch;
   kp.off_z = kp.off_sc + 16 * kMtScalePitch;
   kp.stage_bytes = int(r128(size_t(kp.off_z) + 16 * kMtZeroPitch));
-  const int64_t units = rb_max * kp.nkc;
   const int ow_es = a.ow_dtype == SPECTRA_DT_F32 ? 4 : 2;
   const bool ow_contig = a.n_out > 0 && a.ow_cs == 1 && a.ow_rs == a.n_out && al16(a.ow);
-  for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
-    size_t o = off;
-    kp.off_ow = -1;
-    if (try_ow) {
-      kp.off_ow = int(o);
-      o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
+  // Two compute groups on alternate stages (16 warps hide the shared-memory
+  // and MMA latencies better than 8) while the ring stays >= 4 stages deep;
+  // otherwise one group with the deeper ring.
+  for (int ng = units >= 4 ? 2 : 1; ng >= 1; --ng) {
+    kp.ng = ng;
+    const size_t ow_base = r16(red_base + size_t(ng * kMtGroupWarps) * kp.rows_max * kMtTok * 4);
+    for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
+      size_t o = ow_base;
+      kp.off_ow = -1;
+      if (try_ow) {
+        kp.off_ow = int(o);
+        o = r16(o + size_t(kp.rows_max) * a.n_out * ow_es + 32);
+      }
+      kp.off_stage = int(r128(o));
+      if (size_t(kp.off_stage) >= kMtSmem) continue;
+      int64_t ns = std::min<int64_t>({int64_t(kMtMaxStages), int64_t((kMtSmem - kp.off_stage) / kp.stage_bytes),
+                                      units});
+      if (ng == 2) {
+        ns &= ~int64_t(1);  // a ring slot's consecutive stages belong to one group
+        if (ns < 4) continue;
+      }
+      if (ns < std::min<int64_t>(2, units)) continue;
+      kp.ns = int(ns);
+      smem = size_t(kp.off_stage) + size_t(ns) * kp.stage_bytes;
+      return true;
     }
-    kp.off_stage = int(r128(o));
-    if (size_t(kp.off_stage) >= kMtSmem) continue;
-    const int64_t ns = std::min<int64_t>({int64_t(kMtMaxStages), int64_t((kMtSmem - kp.off_stage) / kp.stage_bytes),
-                                          units});
-    if (ns < std::min<int64_t>(2, units)) continue;
-    kp.ns = int(ns);
-    smem = size_t(kp.off_stage) + size_t(ns) * kp.stage_bytes;
-    return true;
   }
   return false;
 }
@@ -502,9 +528,9 @@ bool encode_mt_maps(const GemmArgs& a, MtMaps& maps) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool BF16>
+template <bool BF16, int NG>
 int launch_mt(const MtMaps& maps, const MtParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
-  auto kern = gemv_mt_kernel<BF16>;
+  auto kern = gemv_mt_kernel<BF16, NG>;
   static PerContextOnce attrs;
   cudaError_t e = attrs.run(dev, [&] {
     cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMtSmem));
@@ -515,7 +541,7 @@ int launch_mt(const MtMaps& maps, const MtParams& kp, int64_t grid, size_t smem,
   if (e != cudaSuccess) return cuda_status(e);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(kMtThreads);
+  cfg.blockDim = dim3((NG * kMtGroupWarps + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -543,8 +569,10 @@ int launch_gemv_mt(const GemmArgs& a, cudaStream_t st) {
   MtMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (!encode_mt_maps(a, maps)) return SPECTRA_ERR_UNSUPPORTED;
-  return a.a_dtype == SPECTRA_DT_BF16 ? launch_mt<true>(maps, kp, grid, smem, dev, st)
-                                      : launch_mt<false>(maps, kp, grid, smem, dev, st);
+  const bool bf = a.a_dtype == SPECTRA_DT_BF16;
+  if (kp.ng == 2)
+    return bf ? launch_mt<true, 2>(maps, kp, grid, smem, dev, st) : launch_mt<false, 2>(maps, kp, grid, smem, dev, st);
+  return bf ? launch_mt<true, 1>(maps, kp, grid, smem, dev, st) : launch_mt<false, 1>(maps, kp, grid, smem, dev, st);
 }
 
 }  // namespace spectra
@@ -594,5 +622,6 @@ extern "C" SPECTRA_API int spectra_gemm_small_m_plan(int64_t M, int64_t N, int64
   out[2] = ok ? int64_t(smem) : 0;
   out[3] = ok ? kp.ns : 0;
   out[4] = ok ? (kp.off_ow >= 0 ? 1 : 0) : 0;
+  out[5] = ok ? kp.ng : 0;
   return SPECTRA_OK;
 }

@@ -77,6 +77,7 @@ struct PfParams {
   int ns;                          // ring stages
   int kc, nkc;                     // input features per stage (a multiple of 512), stages per row block
   int off_sc, off_z, stage_bytes;  // offsets inside one stage (codes at 0)
+  int cs, ss, zs;                  // staged row pitches (bytes) of codes, scales, zero points
   int off_x, off_xsum, off_xos, off_red, off_ow, off_stage;
   int rows_max;
   int vec_x;                       // x contiguous and 16-byte aligned
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
       uint32_t ph = 0;
       int issued = 0;
       bool ok = true;
-      const uint32_t tma_tx = 16u * uint32_t(kp.kc / 2 + kp.kc / 16 + kp.kc / 32);  // full boxes (OOB rows: zeros)
+      const uint32_t tma_tx = 16u * uint32_t(kp.cs + kp.ss + kp.zs);  // full boxes (OOB rows and columns: zeros)
       const int nkc = CHUNKED ? kp.nkc : 1;
       for (int rb = 0; rb < nrb && ok; ++rb) {
         const int64_t row0 = r_begin + int64_t(rb) * 16;
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
           uint8_t* st = smem + kp.off_stage + s * kp.stage_bytes;
           if constexpr (CHUNKED) {
             mbar_arrive_expect_tx(&full_bar[s], tma_tx);
-            tma_load_2d_hint(st, &maps.c, ch * (kp.kc / 8), int(row0), &full_bar[s], policy);
+            tma_load_2d_hint(st, &maps.c, ch * (kp.kc / 16), int(row0), &full_bar[s], policy);
             tma_load_2d_hint(st + kp.off_sc, &maps.s, ch * (kp.kc / 32), int(row0), &full_bar[s], policy);
             tma_load_2d_hint(st + kp.off_z, &maps.z, ch * (kp.kc / 32), int(row0), &full_bar[s], policy);
           } else {
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__((NG * kPfGroupWarps + 1) * 32, NG == 1 ? 2 : 1
   const int KB = p.K >> 8;                               // 256-feature units per row
   const int kc = CHUNKED ? kp.kc : p.K;                 // features per stage
   const int KBc = kc >> 8;                               // 256-feature units per stage
-  const int cs = kc / 2, ss = kc / 16, zs = kc / 32;     // stage row strides (bytes)
+  const int cs = kp.cs, ss = kp.ss, zs = kp.zs;          // stage row pitches (bytes)
   const int nkc = CHUNKED ? kp.nkc : 1;
   const int grp = NG == 1 ? 0 : warp / kPfGroupWarps;  // compute group, and warp inside it
   const int w8 = NG == 1 ? warp : warp % kPfGroupWarps;
@@ -608,23 +609,24 @@ int launch_pf(const PfMaps<true>& all_maps, const PfParams& kp, int64_t grid, si
 
 // Tensor maps of the three weight tensors for [16 rows x kc features] boxes:
 // codes as 32-bit words, scales as 16-bit, zero points as bytes.
-bool encode_stage_maps(const GemvArgs& a, int kc, PfMaps<true>& maps) {
+bool encode_stage_maps(const GemvArgs& a, const PfParams& kp, PfMaps<true>& maps) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   const int G = a.K / kGroup;
   cuuint32_t es[2] = {1, 1};
-  cuuint64_t dc[2] = {cuuint64_t(a.K / 8), cuuint64_t(a.N)}, sc[1] = {cuuint64_t(a.w_rs)};
-  cuuint32_t bc[2] = {cuuint32_t(kc / 8), 16};
+  // codes as 64-bit elements: a box row of cs bytes (the chunk's kc/2 plus the pad)
+  cuuint64_t dc[2] = {cuuint64_t(a.K / 16), cuuint64_t(a.N)}, sc[1] = {cuuint64_t(a.w_rs)};
+  cuuint32_t bc[2] = {cuuint32_t(kp.cs / 8), 16};
   cuuint64_t dg[2] = {cuuint64_t(G), cuuint64_t(a.N)};
   cuuint64_t ss[1] = {cuuint64_t(a.s_rs) * 2}, zs[1] = {cuuint64_t(a.z_rs)};
-  cuuint32_t bg[2] = {cuuint32_t(kc / kGroup), 16};
-  return enc(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(a.packed), dc, sc, bc, es,
+  cuuint32_t bs[2] = {cuuint32_t(kp.ss / 2), 16}, bz[2] = {cuuint32_t(kp.zs), 16};
+  return enc(&maps.c, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(a.packed), dc, sc, bc, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
-         enc(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<__half*>(a.scales), dg, ss, bg, es,
+         enc(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<__half*>(a.scales), dg, ss, bs, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
-         enc(&maps.z, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.zeros), dg, zs, bg, es,
+         enc(&maps.z, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.zeros), dg, zs, bz, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -695,9 +697,19 @@ bool plan_gemv_pf(const GemvArgs& a, int sms, PfParams& kp, PfPlan& pl) {
     if (chunked && !pitches16) break;
     kp.kc = chunked ? std::min(a.K, kPfChunk) : a.K;
     kp.nkc = (a.K + kp.kc - 1) / kp.kc;
-    kp.off_sc = 16 * (kp.kc / 2);                    // codes [16][kc/2 B]
-    kp.off_z = kp.off_sc + 16 * (kp.kc / 16);        // scales [16][kc/16 B]
-    const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(kp.kc / kGroup));  // zero points [16][kc/32 B]
+    // Chunked stages are tensor-map boxes 16 bytes wider than the chunk's data
+    // (the extra bytes are never read): row pitches kc/2 + 16, kc/16 + 16 and
+    // kc/32 + 16 put the 16 rows of a stage in different shared-memory bank
+    // groups, so the lanes of a warp, which read 8 rows at one column, do not
+    // conflict (with power-of-two pitches scales conflicted 8-way, zero points
+    // 4-way, codes 2-way).  Whole-row-block stages keep the tensors' own pitches.
+    const int pad = chunked ? 16 : 0;
+    kp.cs = kp.kc / 2 + pad;
+    kp.ss = kp.kc / 16 + pad;
+    kp.zs = kp.kc / 32 + pad;
+    kp.off_sc = 16 * kp.cs;                          // codes [16][cs B]
+    kp.off_z = kp.off_sc + 16 * kp.ss;               // scales [16][ss B]
+    const size_t sb = r128(size_t(kp.off_z) + 16 * size_t(kp.zs));  // zero points [16][zs B]
     kp.stage_bytes = int(sb);
     const int64_t units = rb_max * kp.nkc;
     // Two compute groups (16 warps) on alternate stages when the CTA owns its
@@ -771,7 +783,7 @@ int launch_gemv_pf(const GemvArgs& a, cudaStream_t st) {
   if (!plan_gemv_pf(a, device_sms(dev), kp, pl)) return SPECTRA_ERR_UNSUPPORTED;
   PfMaps<true> maps;
   memset(&maps, 0, sizeof(maps));
-  if (pl.chunked && !encode_stage_maps(a, kp.kc, maps)) return SPECTRA_ERR_UNSUPPORTED;
+  if (pl.chunked && !encode_stage_maps(a, kp, maps)) return SPECTRA_ERR_UNSUPPORTED;
   const bool bf = a.x_dtype == SPECTRA_DT_BF16;
   if (pl.chunked) {
     if (pl.ng == 2)

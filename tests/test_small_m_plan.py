@@ -9,7 +9,7 @@ from spectra_b200 import _lib as L
 
 
 def plan(M, N, K, n_out, a_dt=L.DT_BF16, ow_dt=L.DT_BF16, sms=148):
-    out = np.zeros(5, np.int64)
+    out = np.zeros(6, np.int64)
     st = L.lib().spectra_gemm_small_m_plan(M, N, K, n_out, a_dt, ow_dt, sms, out.ctypes.data_as(ctypes.c_void_p))
     return st, out
 
@@ -44,10 +44,13 @@ def test_plan_invariants_over_shapes():
                 assert smem <= 220 * 1024
                 units = -(-nblk // grid) * -(-K // 2048)
                 assert 1 <= ns <= 8 and ns >= min(2, units)
+                assert out[5] in (1, 2)
+                if out[5] == 2:  # two groups alternate stages: an even ring of >= 4
+                    assert ns % 2 == 0 and ns >= 4
 
 
 def test_plan_rejects_bad_arguments():
-    out = np.zeros(5, np.int64)
+    out = np.zeros(6, np.int64)
     lib = L.lib()
     assert lib.spectra_gemm_small_m_plan(2, 64, 512, 0, L.DT_BF16, L.DT_BF16, 148, None) == L.ERR_NULL_POINTER
     assert plan(0, 64, 512, 0)[0] == L.ERR_SHAPE
