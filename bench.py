@@ -328,6 +328,87 @@ def t3_compressed(K: int, N: int, seed: int, dev):
     return c
 
 
+def ops_sweep(dev) -> dict:
+    """The kernels around the linear path, each on a
+    decode- or load-sized workload: CUDA events around a CUDA graph of `reps`
+    calls, inputs larger than L2 where the operation is a stream (rotated
+    copies otherwise), GB/s of algorithmic bytes and the fraction of the
+    measured HBM copy bandwidth."""
+    from spectra_b200 import compress as C
+    from spectra_b200 import kernels as SK
+    from spectra_b200 import kvcache as KV
+    peak, _ = measured_peaks()
+    g = torch.Generator(device=dev).manual_seed(7)
+    res = []
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize(dev)
+        gr = capture(lambda: [fn() for _ in range(reps)], dev)
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        dt = time_events(lambda: gr.replay(), dev) / reps
+        del gr
+        return dt
+
+    def add(name, shape, nbytes, dt, note=""):
+        r = {"op": name, "shape": shape, "us": round(dt * 1e6, 2), "gbs": round(nbytes / dt / 1e9, 1),
+             "hbm_frac": round(nbytes / dt / 1e9 / peak, 3)}
+        if note:
+            r["note"] = note
+        res.append(r)
+
+    # GPU quantiser: fp16 [8192 x 8192] (134 MB > L2) -> codes, scales, both zero-point forms
+    w = (torch.randn(8192, 8192, generator=g, device=dev) * 0.02).to(torch.float16)
+    nb = w.numel() * 2 + w.numel() // 2 + (w.numel() // 32) * 3 + w.numel() // 64
+    add("quantize_group32", "8192x8192 fp16", nb, timed(lambda: C.quantize_group32(w), 3))
+    _, _, _, pz = C.quantize_group32(w)
+    del w
+    # load-time zero-point unpack: the lm_head's [128256, 128] packed bytes (copies rotated past L2)
+    pzs = [torch.randint(0, 256, (128256, 128), generator=g, device=dev, dtype=torch.uint8) for _ in range(8)]
+    it = iter(range(10 ** 9))
+    add("unpack_zeros", "128256 x 256 groups", 128256 * 128 * 3,
+        timed(lambda: C.unpack_zeros(pzs[next(it) % 8], 8192), 16), "8 copies rotated")
+    del pzs, pz
+    # INT4 KV cache: one layer's keys of a 32768-token bf16 cache, 8 heads x 128 (64 MB)
+    kv = torch.randn(8 * 32768, 128, generator=g, device=dev).to(torch.bfloat16)
+    n = kv.numel()
+    add("kv_quantize", "262144 x 128 bf16", n * 2 + n // 2 + (n // 32) * 3, timed(lambda: KV.kv_quantize(kv), 4))
+    q = KV.kv_quantize(kv)
+    add("kv_dequantize", "262144 x 128 -> bf16", n * 2 + n // 2 + (n // 32) * 3, timed(lambda: KV.kv_dequantize(q), 4))
+    del kv, q
+    # embedding gather of a 1024-token prompt from the Llama-3-8B vocabulary (4096 wide)
+    V, K = 128256, 4096
+    pk = torch.randint(0, 256, (V, K // 2), generator=g, device=dev, dtype=torch.uint8)
+    sc = (torch.rand(V, K // 32, generator=g, device=dev) * 0.02 + 0.001).to(torch.float16)
+    zz = torch.randint(0, 16, (V, K // 32), generator=g, device=dev, dtype=torch.uint8)
+    oi = torch.randperm(K, generator=g, device=dev)[:41].sort().values
+    ow = (torch.randn(V, 41, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ids = torch.randint(0, V, (1, 1024), generator=g, device=dev)
+    row_b = K // 2 + (K // 32) * 3 + 41 * 2
+    add("embedding", "1024 of 128256 x 4096", 1024 * (row_b + K * 2),
+        timed(lambda: SK.embedding(ids, pk, sc, zz, outlier_idx=oi, outlier_w=ow, marlin_layout=True), 8),
+        "rows gathered from a 305 MB table")
+    ids1 = ids[:, :1].contiguous()
+    add("embedding", "1 of 128256 x 4096 (decode)", row_b + K * 2,
+        timed(lambda: SK.embedding(ids1, pk, sc, zz, outlier_idx=oi, outlier_w=ow, marlin_layout=True), 64),
+        "latency-bound")
+    del pk, sc, zz, ow
+    # greedy argmax over the vocabulary, decode (1 row) and a 64-row batch
+    for M in (1, 64):
+        lg = torch.randn(M, 128256, generator=g, device=dev).to(torch.bfloat16)
+        add("argmax", f"{M} x 128256 bf16", lg.numel() * 2, timed(lambda: SK.argmax(lg), 32),
+            "latency-bound" if M == 1 else "")
+    # FWHT of activation rows (the optional GEMV prologue)
+    for M, nn in ((1, 8192), (256, 4096)):
+        xa = torch.randn(M, nn, generator=g, device=dev).to(torch.bfloat16)
+        add("fwht", f"{M} x {nn} bf16", xa.numel() * 4, timed(lambda: SK.fwht(xa), 32),
+            "latency-bound" if M == 1 else "")
+    torch.cuda.empty_cache()
+    return {"unit": "GB/s of algorithmic bytes; hbm_frac of the measured copy bandwidth",
+            "results": res}
+
+
 def sharded_sweep(world: int, dev, exchange: str = "auto") -> dict:
     """BASELINE config 5 at the job's world size: each Llama-3-70B linear
     column-sharded over the ranks (``spectra_b200.sharded.ShardedW4A16Linear``:
@@ -935,6 +1016,7 @@ def run_gpu(args, world, rank, local):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
+    ops = ops_sweep(dev) if not args.no_ops_sweep else None
     cfg4 = config4_decode(dev, compile_model=not args.config4_eager) if (not args.no_config4 and world == 1) else None
     shard = sharded_sweep(world, dev) if not args.no_sharded_sweep else None
 
@@ -971,6 +1053,7 @@ def run_gpu(args, world, rank, local):
             "cpu_baseline": cpu,
             "gemm_sweep": sweep,
             "config4_decode": cfg4,
+            "ops_sweep": ops,
             "sharded_sweep": shard,
         }
         print(json.dumps(line), flush=True)
@@ -991,6 +1074,7 @@ def main():
     ap.add_argument("--config4-eager", action="store_true",
                     help="run the config-4 model eagerly instead of compiling its non-linear parts with "
                          "torch.compile as the reference engine's loader does")
+    ap.add_argument("--no-ops-sweep", action="store_true", help="skip the sweep of the kernels around the linear path")
     ap.add_argument("--exchange", choices=["auto", "p2p", "collective"], default="auto",
                     help="N > 1: the sharded layers' all-gather (auto: the NVLink peer-memory exchange kernel)")
     ap.add_argument("--no-sharded-sweep", action="store_true",
