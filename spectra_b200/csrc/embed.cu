@@ -16,6 +16,7 @@
 // in torch).  One cluster of 8 CTAs per row; `idx_offset` turns a shard's local index into
 // the layer's row index, so the N-sharded lm_head reduces (value, index)
 // pairs across ranks instead of gathering every logit.
+#include <algorithm>
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -61,8 +62,29 @@ __global__ void __launch_bounds__(kEmbedThreads) embedding_kernel(EmbedArgs a) {
       for (int i = 0; i < kGroup; ++i) v[i] = 0.f;
     }
     const int64_t base = t * a.out_rs + int64_t(g) * kGroup;
+    if (a.vec_out) {
+      // 16-bit output, 16-byte aligned rows: four 16-byte stores
+      uint32_t o[16];
 #pragma unroll
-    for (int i = 0; i < kGroup; ++i) store_from_float(a.out, base + i, a.out_dtype, v[i]);
+      for (int i = 0; i < 16; ++i) {
+        const float lo = v[2 * i], hi = v[2 * i + 1];
+        uint32_t bl, bh;
+        if (a.out_dtype == SPECTRA_DT_BF16) {
+          bl = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+          bh = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+        } else {
+          bl = __half_as_ushort(__float2half_rn(lo));
+          bh = __half_as_ushort(__float2half_rn(hi));
+        }
+        o[i] = bl | (bh << 16);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + base);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) dst[q4] = make_uint4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kGroup; ++i) store_from_float(a.out, base + i, a.out_dtype, v[i]);
+    }
   }
   if (a.n_out > 0 && valid) {
     __syncthreads();  // the outlier columns overwrite what the loop above stored
@@ -196,10 +218,16 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(ArgmaxArgs a) {
 
 }  // namespace
 
-int launch_embedding(const EmbedArgs& a, cudaStream_t st) {
+int launch_embedding(EmbedArgs a, cudaStream_t st) {
   if (a.T == 0) return SPECTRA_OK;
   if (a.T > int64_t(INT32_MAX)) return SPECTRA_ERR_SHAPE;
-  embedding_kernel<<<unsigned(a.T), kEmbedThreads, 0, st>>>(a);
+  // 16-byte stores when the output rows allow them; one thread per group
+  // (CTAs no wider than the row's groups)
+  a.vec_out = (a.out_dtype == SPECTRA_DT_BF16 || a.out_dtype == SPECTRA_DT_F16) &&
+              reinterpret_cast<uintptr_t>(a.out) % 16 == 0 && (a.out_rs * 2) % 16 == 0;
+  const int G = int(a.K / kGroup);
+  const int threads = std::max(32, std::min(kEmbedThreads, (G + 31) / 32 * 32));
+  embedding_kernel<<<unsigned(a.T), threads, 0, st>>>(a);
   return cuda_status(cudaGetLastError());
 }
 

@@ -130,6 +130,30 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group32_kernel(QuantAr
 }
 
 // Zero points packed two per byte -> one byte per group (low nibble: even group).
+// Vector path: 8 packed bytes -> 16 zero points per item (rows padded to
+// whole 16-group blocks, 8/16-byte aligned).
+__global__ void unpack_zeros_vec_kernel(UnpackZerosArgs a) {
+  const int blocks = a.G / 16;
+  const int64_t total = a.N * int64_t(blocks);
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t n = t / blocks;
+    const int b = int(t - n * blocks);
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(a.packed_zeros + n * a.pz_rs) + b);
+    uint32_t o[4];
+    const uint32_t in[2] = {w.x, w.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t lo = in[i] & 0x0F0F0F0Fu, hi = (in[i] >> 4) & 0x0F0F0F0Fu;
+      uint32_t r0, r1;  // {b0.lo, b0.hi, b1.lo, b1.hi}, {b2.lo, b2.hi, b3.lo, b3.hi}
+      asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(r0) : "r"(lo), "r"(hi));
+      asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(r1) : "r"(lo), "r"(hi));
+      o[2 * i] = r0;
+      o[2 * i + 1] = r1;
+    }
+    reinterpret_cast<uint4*>(a.zeros + n * a.z_rs)[b] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 __global__ void unpack_zeros_kernel(UnpackZerosArgs a) {
   const int64_t total = a.N * int64_t(a.G);
   for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += int64_t(gridDim.x) * blockDim.x) {
@@ -169,6 +193,12 @@ int launch_unpack_zeros(const UnpackZerosArgs& a, cudaStream_t st) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
+  const bool vec = a.G % 16 == 0 && a.pz_rs % 8 == 0 && a.z_rs % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.packed_zeros) % 8 == 0 && reinterpret_cast<uintptr_t>(a.zeros) % 16 == 0;
+  if (vec) {
+    unpack_zeros_vec_kernel<<<grid_for(a.N * int64_t(a.G / 16), 256, dev), 256, 0, st>>>(a);
+    return cuda_status(cudaGetLastError());
+  }
   const int grid = grid_for(a.N * int64_t(a.G), 256, dev);
   unpack_zeros_kernel<<<grid, 256, 0, st>>>(a);
   return cuda_status(cudaGetLastError());

@@ -50,8 +50,9 @@ struct EmbedArgs {
   const void* ow; int ow_dtype; int64_t ow_rs;        // [V, n_out]
   void* out; int out_dtype; int64_t out_rs;           // [T, K]
   int64_t V; int K; int layout;
+  bool vec_out;                                       // 16-byte stores (set by the launcher)
 };
-int launch_embedding(const EmbedArgs& a, cudaStream_t st);
+int launch_embedding(EmbedArgs a, cudaStream_t st);
 
 struct ArgmaxArgs {
   const void* x; int x_dtype; int64_t x_rs;  // [M, N]

@@ -47,6 +47,17 @@ struct Num<__half> {
 };
 
 template <typename T>
+__device__ __forceinline__ T bits_lo(uint32_t w) {
+  const uint16_t b = uint16_t(w & 0xFFFFu);
+  return *reinterpret_cast<const T*>(&b);
+}
+template <typename T>
+__device__ __forceinline__ T bits_hi(uint32_t w) {
+  const uint16_t b = uint16_t(w >> 16);
+  return *reinterpret_cast<const T*>(&b);
+}
+
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(kKvThreads) kv_quantize_kernel(KvQuantArgs a) {
   const int G = (a.D + kGroup - 1) / kGroup;
   const int64_t total = a.rows * G;
@@ -57,10 +68,26 @@ __global__ void __launch_bounds__(kKvThreads) kv_quantize_kernel(KvQuantArgs a) 
     const int g = int(u - r * G);
     const T* row = t + r * a.D;
     float v[kGroup];
+    if (VEC) {
+      // whole groups, 16-byte aligned: four 16-byte loads
+      const uint4* src = reinterpret_cast<const uint4*>(row + g * kGroup);
 #pragma unroll
-    for (int i = 0; i < kGroup; ++i) {
-      const int d = g * kGroup + i;
-      v[i] = d < a.D ? Num<T>::f(row[d]) : 0.f;  // zero padding (torch.nn.functional.pad)
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const uint4 w = __ldg(src + q4);
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[8 * q4 + 2 * i] = Num<T>::f(bits_lo<T>(wv[i]));
+          v[8 * q4 + 2 * i + 1] = Num<T>::f(bits_hi<T>(wv[i]));
+        }
+      }
+    }
+    if (!VEC) {
+#pragma unroll
+      for (int i = 0; i < kGroup; ++i) {
+        const int d = g * kGroup + i;
+        v[i] = d < a.D ? Num<T>::f(row[d]) : 0.f;  // zero padding (torch.nn.functional.pad)
+      }
     }
     float lo = v[0], hi = v[0];
 #pragma unroll
@@ -116,6 +143,44 @@ __device__ __forceinline__ void store_t<float>(void* out, int64_t i, float v) {
   reinterpret_cast<float*>(out)[i] = v;
 }
 
+// Vector path (D a multiple of 8): four threads per group, eight values each
+// (bytes 4qq..4qq+3 of the group's codes: elements 8qq..8qq+7), one or two
+// 16-byte stores -- the four threads of a group write 64 contiguous bytes.
+template <typename T>
+__global__ void __launch_bounds__(kKvThreads) kv_dequantize_vec_kernel(KvDequantArgs a) {
+  const int G = (a.D + kGroup - 1) / kGroup;
+  const int64_t total = a.rows * G * 4;
+  for (int64_t it = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; it < total; it += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t u = it >> 2;
+    const int qq = int(it & 3);
+    const int64_t r = u / G;
+    const int g = int(u - r * G);
+    const int d0 = g * kGroup + qq * 8;
+    if (d0 >= a.D) continue;
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(a.packed + u * kGroupBytes) + qq);
+    const float s = __half2float(__ushort_as_half(__ldg(a.scales + u)));
+    const float z = float(__ldg(a.zeros + u));
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(float((w >> (4 * j)) & 0xFu) - z, s);  // element 2b: low nibble of byte b
+    T* dst = reinterpret_cast<T*>(a.out) + r * a.D + d0;
+    if constexpr (sizeof(T) == 4) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        T lo, hi;
+        store_t<T>(&lo, 0, v[2 * j]);
+        store_t<T>(&hi, 0, v[2 * j + 1]);
+        o[j] = uint32_t(*reinterpret_cast<const uint16_t*>(&lo)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+      }
+      *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kKvThreads) kv_dequantize_kernel(KvDequantArgs a) {
   const int G = (a.D + kGroup - 1) / kGroup;
@@ -151,10 +216,19 @@ int launch_kv_quantize(const KvQuantArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return cuda_status(e);
   const int G = (a.D + kGroup - 1) / kGroup;
   const int grid = kv_grid(a.rows * G, dev);
-  if (a.t_dtype == SPECTRA_DT_BF16)
-    kv_quantize_kernel<__nv_bfloat16><<<grid, kKvThreads, 0, st>>>(a);
-  else
-    kv_quantize_kernel<__half><<<grid, kKvThreads, 0, st>>>(a);
+  // whole groups on 16-byte boundaries: 16-byte loads
+  const bool vec = a.D % kGroup == 0 && reinterpret_cast<uintptr_t>(a.t) % 16 == 0;
+  if (a.t_dtype == SPECTRA_DT_BF16) {
+    if (vec)
+      kv_quantize_kernel<__nv_bfloat16, true><<<grid, kKvThreads, 0, st>>>(a);
+    else
+      kv_quantize_kernel<__nv_bfloat16, false><<<grid, kKvThreads, 0, st>>>(a);
+  } else {
+    if (vec)
+      kv_quantize_kernel<__half, true><<<grid, kKvThreads, 0, st>>>(a);
+    else
+      kv_quantize_kernel<__half, false><<<grid, kKvThreads, 0, st>>>(a);
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -163,6 +237,18 @@ int launch_kv_dequantize(const KvDequantArgs& a, cudaStream_t st) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   const int G = (a.D + kGroup - 1) / kGroup;
+  const bool vec = a.D % 8 == 0 && reinterpret_cast<uintptr_t>(a.out) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.packed) % 4 == 0;
+  if (vec) {
+    const int gv = kv_grid(a.rows * G * 4, dev);
+    if (a.out_dtype == SPECTRA_DT_BF16)
+      kv_dequantize_vec_kernel<__nv_bfloat16><<<gv, kKvThreads, 0, st>>>(a);
+    else if (a.out_dtype == SPECTRA_DT_F16)
+      kv_dequantize_vec_kernel<__half><<<gv, kKvThreads, 0, st>>>(a);
+    else
+      kv_dequantize_vec_kernel<float><<<gv, kKvThreads, 0, st>>>(a);
+    return cuda_status(cudaGetLastError());
+  }
   const int grid = kv_grid(a.rows * G, dev);
   if (a.out_dtype == SPECTRA_DT_BF16)
     kv_dequantize_kernel<__nv_bfloat16><<<grid, kKvThreads, 0, st>>>(a);
