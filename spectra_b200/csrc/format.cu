@@ -67,10 +67,25 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_group32_kernel(QuantAr
       if (g >= G) break;
       float v[kGroup];
       const uint32_t m = out_mask[g];  // group g covers features 32g..32g+31: one mask word
+      if (a.w_vec) {
+        // the group's 32 values by 16-byte loads
+        constexpr int kWords = kGroup * int(sizeof(T)) / 4;
+        uint32_t wd[kWords];
+        const uint4* src = reinterpret_cast<const uint4*>(row + int64_t(g) * kGroup);
 #pragma unroll
-      for (int i = 0; i < kGroup; ++i) {
-        const float x = to_f32(row[int64_t(g) * kGroup + i]);
-        v[i] = ((m >> i) & 1u) ? 0.f : x;
+        for (int q4 = 0; q4 < kWords / 4; ++q4) {
+          const uint4 u4 = __ldg(src + q4);
+          wd[4 * q4] = u4.x; wd[4 * q4 + 1] = u4.y; wd[4 * q4 + 2] = u4.z; wd[4 * q4 + 3] = u4.w;
+        }
+        const T* vals = reinterpret_cast<const T*>(wd);
+#pragma unroll
+        for (int i = 0; i < kGroup; ++i) v[i] = ((m >> i) & 1u) ? 0.f : to_f32(vals[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < kGroup; ++i) {
+          const float x = to_f32(row[int64_t(g) * kGroup + i]);
+          v[i] = ((m >> i) & 1u) ? 0.f : x;
+        }
       }
       float lo = v[0], hi = v[0];
 #pragma unroll
@@ -172,10 +187,12 @@ int grid_for(int64_t work, int threads, int dev) {
 
 }  // namespace
 
-int launch_quantize_group32(const QuantArgs& a, cudaStream_t st) {
+int launch_quantize_group32(QuantArgs a, cudaStream_t st) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
+  const int64_t es = a.w_dtype == SPECTRA_DT_F32 ? 4 : 2;
+  a.w_vec = reinterpret_cast<uintptr_t>(a.w) % 16 == 0 && (a.w_rs * es) % 16 == 0 ? 1 : 0;
   const size_t smem = size_t((a.K + 31) / 32) * 4;
   if (smem > 48 * 1024) return SPECTRA_ERR_SHAPE;  // K <= 393216
   const int64_t pairs = (int64_t(a.K / kGroup) + 1) / 2;

@@ -10,6 +10,7 @@ namespace spectra {
 // Group-32 INT4 quantiser (format.cu).
 struct QuantArgs {
   const void* w; int w_dtype; int64_t w_rs;  // [N, K] source weights
+  int w_vec;                                  // 16-byte aligned rows (set by the launcher)
   const void* idx; int idx_dtype; int n_out;  // outlier columns (read as 0), may be empty
   uint8_t* packed; int64_t p_rs; int packed_vec;  // [N, K/2]; packed_vec: 16-byte aligned rows
   uint16_t* scales; int64_t s_rs;             // [N, K/32] fp16
@@ -17,7 +18,7 @@ struct QuantArgs {
   uint8_t* packed_zeros; int64_t pz_rs;       // [N, ceil(K/64)] or NULL
   int N, K, layout;
 };
-int launch_quantize_group32(const QuantArgs& a, cudaStream_t st);
+int launch_quantize_group32(QuantArgs a, cudaStream_t st);
 
 struct UnpackZerosArgs {
   const uint8_t* packed_zeros; int64_t pz_rs;  // [N, ceil(G/2)]
