@@ -585,6 +585,111 @@ def config4_decode(dev, prompt_len: int = 1024, new_tokens: int = 256, compile_m
                    "token as the engine's decode loop does; CUDA events around prefill and around the decode loop"}
 
 
+
+def config4_decode_sharded(dev, world: int, prompt_len: int = 1024, new_tokens: int = 256,
+                           compile_model: bool = True, exchange: str = "auto") -> dict:
+    """BASELINE config 4 N-sharded: the config-4 model on every rank, its
+    largest layer -- the tied lm_head, 4096 x 128256 -- column-sharded over the
+    ranks (``ShardedW4A16Linear``); each decode token ends with the sharded
+    greedy head (this rank's rows, the argmax kernel, one (value, index) pair
+    exchanged per rank) instead of a full row of logits.  The rest of the
+    model is replicated: its 4096-wide layers are too small to shard (the
+    exchange would cost more than the halved GEMV saves), so tok/s is expected
+    to stay at the 1-GPU figure.  Every rank decodes the same tokens."""
+    from transformers import LlamaConfig, LlamaForCausalLM, StaticCache
+    from spectra_b200.modules import quantize_model
+    from spectra_b200.sharded import ShardedW4A16Linear
+    cfg = LlamaConfig(**LLAMA3_8B)
+    cfg.torch_dtype = torch.bfloat16
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).to(torch.bfloat16)
+    quantize_model(model)
+    model.eval()
+    lm = model.lm_head
+    bias = getattr(lm, "bias", None)
+    head = ShardedW4A16Linear(lm.packed_weight, lm.scales, lm.zeros, lm.outlier_idx, lm.outlier_weight,
+                              bias if isinstance(bias, torch.Tensor) else None, marlin_layout=lm.marlin_layout,
+                              device=dev, exchange=exchange)
+    body = model.model
+    compiled = False
+    if compile_model:
+        try:
+            body = torch.compile(body, mode="default", dynamic=True)
+            compiled = True
+        except Exception:  # noqa: BLE001
+            compiled = False
+    g = torch.Generator(device=dev).manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=g, device=dev)
+    cache = StaticCache(config=cfg, max_cache_len=prompt_len + new_tokens + 8)
+    if hasattr(cache, "early_initialization"):
+        cache.early_initialization(batch_size=1, num_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                                   dtype=torch.bfloat16, device=dev)
+
+    def step(inp, pos):
+        h = body(inp, past_key_values=cache, cache_position=pos, use_cache=True).last_hidden_state
+        return head.greedy(h[:, -1, :])
+
+    with torch.no_grad():
+        try:
+            step(ids, torch.arange(prompt_len, device=dev))
+        except Exception:  # noqa: BLE001 -- compilation failed at its first call: run eager
+            if not compiled:
+                raise
+            body = model.model
+            compiled = False
+            step(ids, torch.arange(prompt_len, device=dev))
+        cache.reset()
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        tok = step(ids, torch.arange(prompt_len, device=dev))
+        b.record()
+        b.synchronize()
+        prefill_s = max_over_ranks(a.elapsed_time(b) / 1e3, world, dev)
+        tokens = [int(tok.item())]
+        static_in = torch.tensor([[tokens[0]]], device=dev)
+        static_pos = torch.tensor([prompt_len], device=dev)
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                static_tok = step(static_in, static_pos)
+        torch.cuda.current_stream(dev).wait_stream(st)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            static_tok = step(static_in, static_pos)
+        upload_graph(graph, dev)
+        torch.cuda.synchronize(dev)
+        for layer in getattr(cache, "layers", []):
+            if isinstance(getattr(layer, "cumulative_length", None), torch.Tensor):
+                layer.cumulative_length.fill_(prompt_len)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        a.record()
+        for i in range(new_tokens - 1):
+            static_pos.fill_(prompt_len + i)
+            graph.replay()
+            tokens.append(int(static_tok.item()))
+            static_in.fill_(tokens[-1])
+        b.record()
+        b.synchronize()
+        decode_s = max_over_ranks(a.elapsed_time(b) / 1e3, world, dev)
+    del graph, static_tok, cache
+    head.close()
+    del head, model, body
+    torch.cuda.empty_cache()
+    return {"model": "Llama-3-8B (random init N(0,0.02), every linear and the embedding in SPECTRA's format)",
+            "gpus": world, "prompt_tokens": prompt_len, "new_tokens": new_tokens, "batch": 1,
+            "decode_tok_s": round((new_tokens - 1) / decode_s, 2),
+            "ms_per_token": round(decode_s / (new_tokens - 1) * 1e3, 4),
+            "prefill_tok_s": round(prompt_len / prefill_s, 1), "first_tokens": tokens[:8], "compiled": compiled,
+            "sharding": f"lm_head 4096x128256 column-sharded over {world} GPUs, greedy by (value, index) pair "
+                        "exchange; the rest of the model replicated",
+            "how": "as config4_decode, with the decode step (model body + sharded greedy head) captured in one "
+                   "CUDA graph per rank; CUDA events, slowest rank"}
+
 METRIC_SHARDED = ("W4A16 GEMV GB/s at M=1, Llama-3-70B linears column-sharded over the job's GPUs "
                   "(8192x8192, 8192x28672, 28672x8192, 8192x128256 lm_head)")
 WORKLOAD_SHARDED = ("Llama-3-70B linears at M=1 (BASELINE config 5: Student-t weights), N-column-sharded "
@@ -718,6 +823,9 @@ def run_sharded(args, world, rank, local):
     peak, peak_kind = measured_peaks()
     clk.stop()
     shard = sharded_sweep(world, dev, args.exchange) if not args.no_sharded_sweep else None
+    cfg4 = None
+    if not args.no_config4:
+        cfg4 = config4_decode_sharded(dev, world, compile_model=not args.config4_eager, exchange=args.exchange)
     h2d = sum(x.numel() * 2 for x in h_x.values())
     if rank == 0:
         line = {
@@ -749,6 +857,7 @@ def run_sharded(args, world, rank, local):
             "clocks": clk.summary(w0, w1),
             "cpu_baseline": None,
             "config5_sharded_layers": shard,
+            "config4_decode_sharded": cfg4,
         }
         print(json.dumps(line), flush=True)
     del timed, warm, e2e_graphable, g_h

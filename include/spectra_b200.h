@@ -121,7 +121,7 @@ SPECTRA_API int spectra_w4a16_dequant(
  *   c[m,n] = sum_k a[m,k] * R((q-z)*s) + sum_j a[m,idx_j] * R(ow[n,j])
  * where R() rounds to a's dtype (the reference's tensor-core operands),
  * accumulated in fp32 and rounded once to c (same dtype as a).  No bias
- * (the engine adds it, spectra/engine.py:122-123).  For M <= 8 with the
+ * (the engine adds it, spectra/engine.py:122-123).  For M <= 16 with the
  * layout spectra_gemm_small_m_plan accepts, a small-M kernel computes the same
  * product with the exact dequantised weights instead of R((q-z)*s) (as the
  * M=1 GEMV does; within the path's tolerance of the rounded form) and uses no
@@ -360,10 +360,11 @@ SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_out, int x_
  * Diagnostic, not a reference interface: whether spectra_w4a16_gemm takes its
  * small-M kernel for an [M, K] x [N, K] product with contiguous, 16-byte
  * aligned operands and n_out outlier columns of ow_dtype stored [N, n_out],
- * on a GPU with `sms` SMs (host only, no GPU).  out[6]: 1 if it does (else all
+ * on a GPU with `sms` SMs (host only, no GPU).  out[7]: 1 if it does (else all
  * zero: the tcgen05 GEMM runs), grid, dynamic shared memory bytes, ring
- * stages, outlier rows staged before the wait (1/0), compute groups.  The kernel takes
- * 2 <= M <= 8, K a multiple of 512, bf16/fp16 activations, when the staged
+ * stages, outlier rows staged before the wait (1/0), compute groups, token
+ * tiles of 8.  The kernel takes
+ * 2 <= M <= 16, K a multiple of 512, bf16/fp16 activations, when the staged
  * activations of all M rows and two weight stages fit in shared memory.
  * SPECTRA_B200_GEMM_SMALL_M=0 in the environment turns it off.
  */

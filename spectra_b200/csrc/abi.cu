@@ -212,7 +212,11 @@ int spectra_w4a16_gemm(
   g.ow = has_out ? outlier_w : nullptr; g.ow_dtype = ow_dtype; g.ow_rs = ow_row_stride; g.ow_cs = ow_col_stride;
   g.c = c; g.c_dtype = c_dtype; g.c_rs = c_row_stride;
   g.M = int(M); g.N = int(N); g.K = int(K); g.layout = layout;
-  if (M <= 8) {  // decode batch sizes: the raw-code small-M kernel when its layout conditions hold
+  {  // the workspace contract does not depend on which kernel runs: checked first, on the host
+    const GemmPlan pl = plan_gemm(M, N, K, n_out);
+    if (pl.S > 1 && (workspace == nullptr || workspace_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
+  }
+  if (M <= 16) {  // decode batch sizes: the raw-code small-M kernel when its layout conditions hold
     const int r = launch_gemv_mt(g, static_cast<cudaStream_t>(stream));
     if (r != SPECTRA_ERR_UNSUPPORTED) return r;
   }

@@ -36,7 +36,7 @@ struct GemmPlan {
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out);
 int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st);
 
-// Small-M GEMM (M = 2..8) on the raw-code tensor-core step (gemv_mt.cu);
+// Small-M GEMM (M = 2..16) on the raw-code tensor-core step (gemv_mt.cu);
 // SPECTRA_ERR_UNSUPPORTED (nothing launched) when the arguments do not meet
 // its conditions, and the tcgen05 GEMM takes the call.
 int launch_gemv_mt(const GemmArgs& a, cudaStream_t st);

@@ -1,4 +1,4 @@
-// Small-M W4A16 GEMM (M = 2..8 token rows) for sm_100a: the decode batch
+// Small-M W4A16 GEMM (M = 2..16 token rows) for sm_100a: the decode batch
 // sizes of the M >= 2 branch (spectra/kernels.py:191-389, batched_w4a16_gemm,
 // which the engine's batched generation reaches with M = 2..4), computed with
 // the M=1 GEMV's raw-code tensor-core step instead of the dequantising tcgen05
@@ -13,7 +13,8 @@
 //   + LOP3 turns a pair of codes into two bf16/fp16 (16 + q) (pair_code), so two
 //   m16n8k16 MMAs cover the group's 32 k.  B (16 k x 8) is dense: column n is
 //   token n's activations at the same k (staged once per call in exactly this
-//   fragment order), so D[row][token] = sum_k (16 + q_k) x_k over the group and
+//   fragment order; M > 8 takes a second tile of 8 tokens on the same A
+//   registers), so D[row][token] = sum_k (16 + q_k) x_k over the group and
 //   y[row][token] += s (D - (16 + z) X_g[token]), X_g the group's activation
 //   sum, in fp32 -- the exact dequantised weights, like the M=1 GEMV (the
 //   reference GEMM rounds them to the compute dtype first; both are within the
@@ -66,14 +67,15 @@ struct MtParams {
   int ns;                   // ring depth
   int off_sc, off_z, stage_bytes;
   int off_xb, xb_tok;       // x fragments [M][G][4] x 16 B, token pitch in bytes
-  int off_xsum;             // [G][8] fp32
-  int off_xos;              // [n_out][8] fp32
-  int off_red;              // [8 warps][rows_max][8] fp32
+  int off_xsum;             // [G][8 nt] fp32
+  int off_xos;              // [n_out][8 nt] fp32
+  int off_red;              // [warps][rows_max][8 nt] fp32
   int off_ow;               // staged outlier weight rows (or -1)
   int off_stage;
   int rows_max;
   int vec_a;                // 16-byte activation loads
   int ng;                   // compute groups (alternate stages)
+  int nt;                   // token tiles of 8
 };
 
 struct MtMaps {
@@ -126,12 +128,13 @@ __device__ __forceinline__ void mt_bar() {
 }
 
 // NG compute groups of 8 warps (group i takes stages i, i + NG, ...) and one
-// producer warp.
-template <bool BF16, int NG>
+// producer warp; NT token tiles of 8 (M <= 8 NT), which share every A operand.
+template <bool BF16, int NG, int NT>
 __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
     gemv_mt_kernel(const __grid_constant__ MtMaps maps, const __grid_constant__ MtParams kp) {
   using namespace sm100;
   constexpr int kMtWarps = NG * kMtGroupWarps;  // compute warps
+  constexpr int TOK = kMtTok * NT;              // token stride of the per-token shared arrays
   const GemmArgs& p = kp.a;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kMtMaxStages];
@@ -223,13 +226,13 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
   const int rows_max = kp.rows_max;
 
   // the row partials start at zero (shared memory only: before the wait)
-  for (int i = tid; i < kMtWarps * rows_max * kMtTok; i += kCT) red[i] = 0.f;
+  for (int i = tid; i < kMtWarps * rows_max * TOK; i += kCT) red[i] = 0.f;
 
   pdl_wait();  // the activations may be the previous kernel's output
 
   // x at the outlier features, [j][token]
-  for (int i = tid; i < p.n_out * kMtTok; i += kCT) {
-    const int j = i >> 3, t = i & 7;
+  for (int i = tid; i < p.n_out * TOK; i += kCT) {
+    const int j = i / TOK, t = i % TOK;
     float v = 0.f;
     if (t < M) {
       const int64_t k = load_index(p.idx, j, p.idx_dtype);
@@ -268,7 +271,7 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
         X += f.x + f.y;
       }
     }
-    xsum[grp * kMtTok + t] = X;
+    xsum[grp * TOK + t] = X;
     uint4* dst = reinterpret_cast<uint4*>(xb + t * kp.xb_tok + grp * 64);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
@@ -287,15 +290,15 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
       dst[c] = f;
     }
   }
-  for (int i = tid; i < G * kMtTok; i += kCT)
-    if ((i & 7) >= M) xsum[i] = 0.f;
+  for (int i = tid; i < G * TOK; i += kCT)
+    if (i % TOK >= M) xsum[i] = 0.f;
   mt_bar<kCT>();
 
   // ------------------------------------------------------------ main loop
   uint32_t magic_reg;
   asm volatile("mov.b32 %0, %1;" : "=r"(magic_reg) : "n"(BF16 ? 0x41804180u : 0x4C004C00u));  // 16.0 x2
   const int g = lane >> 2, c = lane & 3;
-  const bool tok_ok = g < M;  // this lane's B column is a real token
+  // this lane's B column of tile tt is token g + 8 tt
   // ldmatrix row addresses: lanes 0-7 rows 0-7 / 8-15 rows 8-15 of group gl,
   // 16-31 the same rows of group gl + 1
   const int lm_row = (lane & 7) + 8 * ((lane >> 3) & 1);
@@ -309,7 +312,7 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
   int s = 0, si = 0;
   uint32_t ph = 0;
   for (int rb = 0; rb < nrb; ++rb) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[NT][4] = {};
     for (int ch = 0; ch < kp.nkc; ++ch, ++si) {
       if (NG > 1 && si % NG != grp_id) {
         if (++s == kp.ns) { s = 0; ph ^= 1u; }
@@ -340,23 +343,28 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
               const int gi = 2 * gp + h;
               const int grp = kb * 8 + gi;
               const uint32_t wg = wv[2 * h], wg8 = wv[2 * h + 1];
-              uint32_t bf[4] = {0u, 0u, 0u, 0u};
-              lds128_if(bf, xb + g * kp.xb_tok + grp * 64 + c * 16, tok_ok);
-              float d[4] = {0.f, 0.f, 0.f, 0.f};
-              mma16816<BF16>(d, pair_code<BF16, 0>(wg, magic_reg), pair_code<BF16, 0>(wg8, magic_reg),
-                             pair_code<BF16, 2>(wg, magic_reg), pair_code<BF16, 2>(wg8, magic_reg), bf[0], bf[1]);
-              mma16816<BF16>(d, pair_code<BF16, 1>(wg, magic_reg), pair_code<BF16, 1>(wg8, magic_reg),
-                             pair_code<BF16, 3>(wg, magic_reg), pair_code<BF16, 3>(wg8, magic_reg), bf[2], bf[3]);
-              // d = {D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]}
-              const float2 X = *reinterpret_cast<const float2*>(xsum + grp * kMtTok + 2 * c);
+              const uint32_t a0 = pair_code<BF16, 0>(wg, magic_reg), a1 = pair_code<BF16, 0>(wg8, magic_reg);
+              const uint32_t a2 = pair_code<BF16, 2>(wg, magic_reg), a3 = pair_code<BF16, 2>(wg8, magic_reg);
+              const uint32_t a4 = pair_code<BF16, 1>(wg, magic_reg), a5 = pair_code<BF16, 1>(wg8, magic_reg);
+              const uint32_t a6 = pair_code<BF16, 3>(wg, magic_reg), a7 = pair_code<BF16, 3>(wg8, magic_reg);
               const float s_a = __half2float(__ushort_as_half(uint16_t(sa[gi >> 1] >> (16 * (gi & 1)))));
               const float s_b = __half2float(__ushort_as_half(uint16_t(sb[gi >> 1] >> (16 * (gi & 1)))));
               const float z_a = 16.f + float((za[gi >> 2] >> (8 * (gi & 3))) & 0xFFu);
               const float z_b = 16.f + float((zb[gi >> 2] >> (8 * (gi & 3))) & 0xFFu);
-              acc[0] += s_a * fmaf(-z_a, X.x, d[0]);
-              acc[1] += s_a * fmaf(-z_a, X.y, d[1]);
-              acc[2] += s_b * fmaf(-z_b, X.x, d[2]);
-              acc[3] += s_b * fmaf(-z_b, X.y, d[3]);
+#pragma unroll
+              for (int tt = 0; tt < NT; ++tt) {
+                uint32_t bf[4] = {0u, 0u, 0u, 0u};
+                lds128_if(bf, xb + (g + 8 * tt) * kp.xb_tok + grp * 64 + c * 16, g + 8 * tt < M);
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816<BF16>(d, a0, a1, a2, a3, bf[0], bf[1]);
+                mma16816<BF16>(d, a4, a5, a6, a7, bf[2], bf[3]);
+                // d = {D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]} of tile tt
+                const float2 X = *reinterpret_cast<const float2*>(xsum + grp * TOK + 8 * tt + 2 * c);
+                acc[tt][0] += s_a * fmaf(-z_a, X.x, d[0]);
+                acc[tt][1] += s_a * fmaf(-z_a, X.y, d[1]);
+                acc[tt][2] += s_b * fmaf(-z_b, X.x, d[2]);
+                acc[tt][3] += s_b * fmaf(-z_b, X.y, d[3]);
+              }
             }
           }
         }
@@ -365,10 +373,13 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
       if (lane == 0) mbar_arrive(&empty_bar[s]);
       if (++s == kp.ns) { s = 0; ph ^= 1u; }
     }
-    // this warp's partials of the row block: rows g, g+8, tokens 2c, 2c+1
-    float* rw = red + (int64_t(warp) * rows_max + rb * 16) * kMtTok;
-    *reinterpret_cast<float2*>(rw + g * kMtTok + 2 * c) = make_float2(acc[0], acc[1]);
-    *reinterpret_cast<float2*>(rw + (g + 8) * kMtTok + 2 * c) = make_float2(acc[2], acc[3]);
+    // this warp's partials of the row block: rows g, g+8, tokens 8 tt + 2c, + 1
+    float* rw = red + (int64_t(warp) * rows_max + rb * 16) * TOK;
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+      *reinterpret_cast<float2*>(rw + g * TOK + 8 * tt + 2 * c) = make_float2(acc[tt][0], acc[tt][1]);
+      *reinterpret_cast<float2*>(rw + (g + 8) * TOK + 8 * tt + 2 * c) = make_float2(acc[tt][2], acc[tt][3]);
+    }
   }
 
   // ---------------------------- outlier columns, the partials in order, store
@@ -388,46 +399,49 @@ __global__ void __launch_bounds__((NG * kMtGroupWarps + 1) * 32, 1)
   const uint8_t* ow_rows = smem + (kp.off_ow >= 0 ? kp.off_ow : 0) + (ow_b0 - ow_a0);
   for (int i0 = 0; i0 < nrows; i0 += kCT / tpr) {  // CTA-uniform trips
     const int i = i0 + tid / tpr;
-    float v[kMtTok];
+#pragma unroll 1
+    for (int tt = 0; tt < NT; ++tt) {  // 8 tokens at a time
+      float v[kMtTok];
 #pragma unroll
-    for (int t = 0; t < kMtTok; ++t) v[t] = 0.f;
-    if (i < nrows && ow_ok) {
-      for (int j = sub; j < p.n_out; j += tpr) {
-        float w;
-        if (ow_staged) {
-          const uint8_t* orow = ow_rows + int64_t(i) * row_bytes;
-          w = ow_es == 4 ? reinterpret_cast<const float*>(orow)[j]
-              : p.ow_dtype == SPECTRA_DT_BF16
-                  ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(orow)[j]) << 16)
-                  : __half2float(reinterpret_cast<const __half*>(orow)[j]);
-        } else {
-          w = load_as_float(p.ow, (r_begin + i) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype);
+      for (int t = 0; t < kMtTok; ++t) v[t] = 0.f;
+      if (i < nrows && ow_ok) {
+        for (int j = sub; j < p.n_out; j += tpr) {
+          float w;
+          if (ow_staged) {
+            const uint8_t* orow = ow_rows + int64_t(i) * row_bytes;
+            w = ow_es == 4 ? reinterpret_cast<const float*>(orow)[j]
+                : p.ow_dtype == SPECTRA_DT_BF16
+                    ? __uint_as_float(uint32_t(reinterpret_cast<const uint16_t*>(orow)[j]) << 16)
+                    : __half2float(reinterpret_cast<const __half*>(orow)[j]);
+          } else {
+            w = load_as_float(p.ow, (r_begin + i) * p.ow_rs + int64_t(j) * p.ow_cs, p.ow_dtype);
+          }
+          const float4 x0 = *reinterpret_cast<const float4*>(xos + j * TOK + 8 * tt);
+          const float4 x1 = *reinterpret_cast<const float4*>(xos + j * TOK + 8 * tt + 4);
+          v[0] = fmaf(x0.x, w, v[0]); v[1] = fmaf(x0.y, w, v[1]); v[2] = fmaf(x0.z, w, v[2]); v[3] = fmaf(x0.w, w, v[3]);
+          v[4] = fmaf(x1.x, w, v[4]); v[5] = fmaf(x1.y, w, v[5]); v[6] = fmaf(x1.z, w, v[6]); v[7] = fmaf(x1.w, w, v[7]);
         }
-        const float4 x0 = *reinterpret_cast<const float4*>(xos + j * kMtTok);
-        const float4 x1 = *reinterpret_cast<const float4*>(xos + j * kMtTok + 4);
-        v[0] = fmaf(x0.x, w, v[0]); v[1] = fmaf(x0.y, w, v[1]); v[2] = fmaf(x0.z, w, v[2]); v[3] = fmaf(x0.w, w, v[3]);
-        v[4] = fmaf(x1.x, w, v[4]); v[5] = fmaf(x1.y, w, v[5]); v[6] = fmaf(x1.z, w, v[6]); v[7] = fmaf(x1.w, w, v[7]);
       }
-    }
-    // sum over the row's 8 lanes, transposing: afterwards v[0] of lane
-    // (sub) is the total of token sub
+      // sum over the row's 8 lanes, transposing: afterwards v[0] of lane
+      // (sub) is the total of token 8 tt + sub
 #pragma unroll
-    for (int half = 4; half >= 1; half >>= 1) {
-      const bool up = (lane & half) != 0;
+      for (int half = 4; half >= 1; half >>= 1) {
+        const bool up = (lane & half) != 0;
 #pragma unroll
-      for (int q = 0; q < half; ++q) {
-        const float send = up ? v[q] : v[q + half];
-        const float keep = up ? v[q + half] : v[q];
-        v[q] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+        for (int q = 0; q < half; ++q) {
+          const float send = up ? v[q] : v[q + half];
+          const float keep = up ? v[q + half] : v[q];
+          v[q] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+        }
       }
-    }
-    const int t = sub;
-    if (i < nrows && t < M) {
-      float y = 0.f;
+      const int t = 8 * tt + sub;
+      if (i < nrows && t < M) {
+        float y = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kMtWarps; ++ww) y += red[(int64_t(ww) * rows_max + i) * kMtTok + t];
-      y += v[0];
-      store_from_float(p.c, int64_t(t) * p.c_rs + r_begin + i, p.c_dtype, y);
+        for (int ww = 0; ww < kMtWarps; ++ww) y += red[(int64_t(ww) * rows_max + i) * TOK + t];
+        y += v[0];
+        store_from_float(p.c, int64_t(t) * p.c_rs + r_begin + i, p.c_dtype, y);
+      }
     }
   }
 }
@@ -447,7 +461,7 @@ bool small_m_enabled() {
 // The configuration of the small-M kernel for `a` (no CUDA call); false when
 // it does not take the call (the tcgen05 GEMM does).
 bool plan_gemv_mt(const GemmArgs& a, int sms, MtParams& kp, int64_t& grid, size_t& smem) {
-  if (a.M < 2 || a.M > kMtTok || a.K % 512 != 0 || a.N <= 0 || sms <= 0) return false;
+  if (a.M < 2 || a.M > 2 * kMtTok || a.K % 512 != 0 || a.N <= 0 || sms <= 0) return false;
   if (a.a_dtype != SPECTRA_DT_BF16 && a.a_dtype != SPECTRA_DT_F16) return false;
   if (!al16(a.packed) || !al16(a.scales) || !al16(a.zeros) || a.s_cs != 1 || a.z_cs != 1) return false;
   if (a.w_rs % 16 != 0 || (a.s_rs * 2) % 16 != 0 || a.z_rs % 16 != 0) return false;  // tensor-map pitches
@@ -465,9 +479,11 @@ bool plan_gemv_mt(const GemmArgs& a, int sms, MtParams& kp, int64_t& grid, size_
   kp.xb_tok = G * 64 + 64;  // + 64: tokens start in different bank groups
   off = r16(size_t(a.M) * kp.xb_tok);
   kp.off_xsum = int(off);
-  off = r16(off + size_t(G) * kMtTok * 4);
+  kp.nt = a.M > kMtTok ? 2 : 1;  // token tiles
+  const int tok = kMtTok * kp.nt;
+  off = r16(off + size_t(G) * tok * 4);
   kp.off_xos = int(off);
-  off = r16(off + size_t(a.n_out) * kMtTok * 4);
+  off = r16(off + size_t(a.n_out) * tok * 4);
   kp.off_red = int(off);
   const size_t red_base = off;
   const int64_t units = rb_max * kp.nkc;
@@ -481,7 +497,7 @@ bool plan_gemv_mt(const GemmArgs& a, int sms, MtParams& kp, int64_t& grid, size_
   // otherwise one group with the deeper ring.
   for (int ng = units >= 4 ? 2 : 1; ng >= 1; --ng) {
     kp.ng = ng;
-    const size_t ow_base = r16(red_base + size_t(ng * kMtGroupWarps) * kp.rows_max * kMtTok * 4);
+    const size_t ow_base = r16(red_base + size_t(ng * kMtGroupWarps) * kp.rows_max * tok * 4);
     for (int try_ow = ow_contig ? 1 : 0; try_ow >= 0; --try_ow) {
       size_t o = ow_base;
       kp.off_ow = -1;
@@ -528,9 +544,9 @@ bool encode_mt_maps(const GemmArgs& a, MtMaps& maps) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool BF16, int NG>
+template <bool BF16, int NG, int NT>
 int launch_mt(const MtMaps& maps, const MtParams& kp, int64_t grid, size_t smem, int dev, cudaStream_t st) {
-  auto kern = gemv_mt_kernel<BF16, NG>;
+  auto kern = gemv_mt_kernel<BF16, NG, NT>;
   static PerContextOnce attrs;
   cudaError_t e = attrs.run(dev, [&] {
     cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMtSmem));
@@ -570,9 +586,14 @@ int launch_gemv_mt(const GemmArgs& a, cudaStream_t st) {
   memset(&maps, 0, sizeof(maps));
   if (!encode_mt_maps(a, maps)) return SPECTRA_ERR_UNSUPPORTED;
   const bool bf = a.a_dtype == SPECTRA_DT_BF16;
+  if (kp.nt == 2) {
+    if (kp.ng == 2)
+      return bf ? launch_mt<true, 2, 2>(maps, kp, grid, smem, dev, st) : launch_mt<false, 2, 2>(maps, kp, grid, smem, dev, st);
+    return bf ? launch_mt<true, 1, 2>(maps, kp, grid, smem, dev, st) : launch_mt<false, 1, 2>(maps, kp, grid, smem, dev, st);
+  }
   if (kp.ng == 2)
-    return bf ? launch_mt<true, 2>(maps, kp, grid, smem, dev, st) : launch_mt<false, 2>(maps, kp, grid, smem, dev, st);
-  return bf ? launch_mt<true, 1>(maps, kp, grid, smem, dev, st) : launch_mt<false, 1>(maps, kp, grid, smem, dev, st);
+    return bf ? launch_mt<true, 2, 1>(maps, kp, grid, smem, dev, st) : launch_mt<false, 2, 1>(maps, kp, grid, smem, dev, st);
+  return bf ? launch_mt<true, 1, 1>(maps, kp, grid, smem, dev, st) : launch_mt<false, 1, 1>(maps, kp, grid, smem, dev, st);
 }
 
 }  // namespace spectra
@@ -623,5 +644,6 @@ extern "C" SPECTRA_API int spectra_gemm_small_m_plan(int64_t M, int64_t N, int64
   out[3] = ok ? kp.ns : 0;
   out[4] = ok ? (kp.off_ow >= 0 ? 1 : 0) : 0;
   out[5] = ok ? kp.ng : 0;
+  out[6] = ok ? kp.nt : 0;
   return SPECTRA_OK;
 }

@@ -84,7 +84,7 @@ def small_m_path(M: int, N: int, K: int, n_out: int, a_dtype: str = "bf16", ow_d
     import ctypes
     from spectra_b200 import _lib as L
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
-    out = np.zeros(6, np.int64)
+    out = np.zeros(7, np.int64)
     cd = "bf16" if a_dtype == "bf16" else "f16"
     st = L.lib().spectra_gemm_small_m_plan(M, N, K, n_out, _DT_CODE[cd], _DT_CODE[ow_dtype], sms,
                                           out.ctypes.data_as(ctypes.c_void_p))

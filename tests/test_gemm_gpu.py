@@ -166,10 +166,12 @@ def test_gemm_outlier_counts(n_out):
 @pytest.mark.parametrize("idx_dtype", [torch.int32, torch.int64])
 def test_gemm_outlier_dtypes(ow_dtype, idx_dtype):
     fmt = random_format(256, 512, 9, seed=3, ow_dtype=ow_dtype)
-    a = act(16, 512, seed=3, dtype="bf16")
-    c = run_gemm(fmt, a, idx_dtype=idx_dtype)
-    c_exact, c_round, cd = oracle_gemm(fmt, a)
-    assert_close_to_oracle(out_f64(c), c_exact, c_round, cd, f"{ow_dtype}/{idx_dtype}")
+    for M in (16, 24):  # the small-M kernel, then the tcgen05 GEMM
+        a = act(M, 512, seed=3, dtype="bf16")
+        c = run_gemm(fmt, a, idx_dtype=idx_dtype)
+        oracle = oracle_exact_weights if takes_small_m(fmt, a) else oracle_gemm
+        c_exact, c_round, cd = oracle(fmt, a)
+        assert_close_to_oracle(out_f64(c), c_exact, c_round, cd, f"M={M} {ow_dtype}/{idx_dtype}")
 
 
 def test_gemm_compressed_weights():

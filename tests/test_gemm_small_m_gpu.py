@@ -1,4 +1,4 @@
-"""The small-M GEMM kernel (M = 2..8, gemv_mt.cu) behind batched_w4a16_gemm:
+"""The small-M GEMM kernel (M = 2..16, gemv_mt.cu) behind batched_w4a16_gemm:
 parity with the exact-weights oracle (1 output ulp of the correctly rounded
 exact result, floor 2^-16*||c||_inf) and with the reference GEMM's operand
 rounding (1e-2*||c||_inf), over token counts, Llama shapes, both nibble orders,
@@ -52,7 +52,7 @@ def _shape_of(fmt):
     return fmt["packed"].shape[0], fmt["packed"].shape[1] * 2
 
 
-@pytest.mark.parametrize("M", [2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("M", [2, 3, 4, 5, 6, 7, 8, 9, 12, 15, 16])
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 def test_token_counts(M, dt):
     fmt = random_format(1000, 2048, 21, seed=M, ow_dtype=dt)
@@ -63,7 +63,7 @@ def test_token_counts(M, dt):
 
 
 @pytest.mark.parametrize("K,N,M", [(4096, 4096, 8), (4096, 1024, 4), (4096, 14336, 8), (14336, 4096, 2),
-                                   (14336, 4096, 4), (8192, 8192, 8)])
+                                   (14336, 4096, 4), (8192, 8192, 8), (4096, 4096, 16), (4096, 1024, 13)])
 def test_llama_shapes(K, N, M):
     fmt = random_format(N, K, K // 100, seed=K + N + M, ow_dtype="bf16")
     n_out = int(fmt["outlier_idx"].size)
@@ -82,9 +82,10 @@ def test_llama_shapes(K, N, M):
 @pytest.mark.parametrize("marlin", [True, False])
 def test_ragged_shapes_and_layouts(N, K, marlin):
     fmt = random_format(N, K, min(9, K // 64), seed=N + K, ow_dtype="bf16")
-    assert small_m_path(5, N, K, min(9, K // 64))
-    a = act(5, K, seed=N, dtype="bf16")
-    _check(fmt, a, _run(fmt, a, marlin=marlin), marlin=marlin, what=f"N={N} K={K} marlin={marlin}")
+    for M in (5, 11):
+        assert small_m_path(M, N, K, min(9, K // 64))
+        a = act(M, K, seed=N + M, dtype="bf16")
+        _check(fmt, a, _run(fmt, a, marlin=marlin), marlin=marlin, what=f"N={N} K={K} M={M} marlin={marlin}")
 
 
 @pytest.mark.parametrize("ow_dtype", ["f16", "bf16", "f32"])

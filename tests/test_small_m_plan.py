@@ -9,7 +9,7 @@ from spectra_b200 import _lib as L
 
 
 def plan(M, N, K, n_out, a_dt=L.DT_BF16, ow_dt=L.DT_BF16, sms=148):
-    out = np.zeros(6, np.int64)
+    out = np.zeros(7, np.int64)
     st = L.lib().spectra_gemm_small_m_plan(M, N, K, n_out, a_dt, ow_dt, sms, out.ctypes.data_as(ctypes.c_void_p))
     return st, out
 
@@ -19,7 +19,10 @@ def plan(M, N, K, n_out, a_dt=L.DT_BF16, ow_dt=L.DT_BF16, sms=148):
     (4, 4096, 14336, 143, True), (2, 4096, 14336, 143, True), (8, 8192, 8192, 82, True),
     (8, 4096, 14336, 143, False),   # 8 rows of 14336 activations do not fit beside two stages
     (1, 4096, 4096, 41, False),     # M = 1 is the GEMV's
-    (9, 4096, 4096, 41, False),     # above one MMA token tile: the tcgen05 GEMM
+    (16, 4096, 4096, 41, True),     # two token tiles
+    (12, 1024, 4096, 41, True),
+    (16, 14336, 4096, 41, False),   # 16 rows of activations and the row partials leave no two stages
+    (17, 4096, 4096, 41, False),    # above two token tiles: the tcgen05 GEMM
     (4, 4096, 4000, 40, False),     # K not a multiple of 512
 ])
 def test_which_calls_it_takes(M, N, K, n_out, taken):
@@ -31,7 +34,7 @@ def test_which_calls_it_takes(M, N, K, n_out, taken):
 
 
 def test_plan_invariants_over_shapes():
-    for M in range(2, 9):
+    for M in range(2, 17):
         for K in (512, 1024, 2048, 2560, 4096, 6144, 8192, 14336, 28672):
             for N in (16, 100, 1024, 4099, 14336, 28672, 128256):
                 st, out = plan(M, N, K, min(K // 32, 900))
@@ -45,12 +48,13 @@ def test_plan_invariants_over_shapes():
                 units = -(-nblk // grid) * -(-K // 2048)
                 assert 1 <= ns <= 8 and ns >= min(2, units)
                 assert out[5] in (1, 2)
+                assert out[6] == (2 if M > 8 else 1)
                 if out[5] == 2:  # two groups alternate stages: an even ring of >= 4
                     assert ns % 2 == 0 and ns >= 4
 
 
 def test_plan_rejects_bad_arguments():
-    out = np.zeros(6, np.int64)
+    out = np.zeros(7, np.int64)
     lib = L.lib()
     assert lib.spectra_gemm_small_m_plan(2, 64, 512, 0, L.DT_BF16, L.DT_BF16, 148, None) == L.ERR_NULL_POINTER
     assert plan(0, 64, 512, 0)[0] == L.ERR_SHAPE
