@@ -96,9 +96,6 @@ def dist_setup():
         if backend == "nccl":
             torch.cuda.set_device(local)
             kw["device_id"] = torch.device("cuda", local)
-            # the communicator's init lines (rank count, transports) in the log
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group(backend, timeout=timedelta(seconds=120), **kw)
     return world, rank, local
 
