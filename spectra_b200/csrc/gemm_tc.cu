@@ -713,14 +713,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const int half_cols = kp.MT / 2;
     // accumulator columns c0..c0+7, summed over the issuers in order
+    // (the issuers' loads all in flight before one wait)
     auto acc8 = [&](int c0, float (&v)[8]) {
-      tmem_ld_x8(tmem + lane_base + uint32_t(c0), v);
-      for (int i = 1; i < NI; ++i) {
-        float u8[8];
-        tmem_ld_x8(tmem + lane_base + uint32_t(i * kp.MT + c0), u8);
+      uint32_t r[kMaxIssuers][8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] += u8[e];
-      }
+      for (int i = 0; i < kMaxIssuers; ++i)
+        if (i < NI) tmem_ld_x8_nowait(tmem + lane_base + uint32_t(i * kp.MT + c0), r[i]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[0][e]);
+#pragma unroll
+      for (int i = 1; i < kMaxIssuers; ++i)
+        if (i < NI) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] += __uint_as_float(r[i][e]);
+        }
     };
     // one issuer: 32 columns per TMEM load and one wait per load (a wait per 8
     // columns made the epilogue ~6 us of a 55 us launch at MT = 256)
