@@ -371,6 +371,23 @@ SPECTRA_API int spectra_gemv_pf_plan(int64_t N, int64_t K, int64_t n_out, int x_
 SPECTRA_API int spectra_gemm_small_m_plan(int64_t M, int64_t N, int64_t K, int64_t n_out, int a_dtype, int ow_dtype,
                                           int sms, int64_t* out);
 
+/*
+ * Diagnostic, not a reference interface: the tcgen05 GEMM's plan for an
+ * [M, K] x [N, K] product with n_out outlier columns (host only, no GPU).
+ * out[8]: token tile MT, token chunks, weight tiles, K splits, SM pairs
+ * (1/0: tiles of >= 128 tokens on two-CTA clusters, cta_group::2), CTAs per
+ * chunk, activation stages, workspace bytes.  The SM pairs are off unless
+ * SPECTRA_B200_GEMM_PAIR=1 is in the environment (read once per process).
+ */
+SPECTRA_API int spectra_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t n_out, int64_t* out);
+
+/*
+ * Diagnostic: how many two-CTA clusters of the SM-pair GEMM kernel the current
+ * device holds at once (cudaOccupancyMaxActiveClusters at the kernel's largest
+ * shared-memory size).  The plan assumes all SMs pair up: 74 on a B200.
+ */
+SPECTRA_API int spectra_gemm_pair_capacity(int* clusters);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

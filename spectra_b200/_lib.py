@@ -49,6 +49,8 @@ PROTOTYPES = {
     # diagnostic: the M=1 GEMV's configuration for a shape (host only)
     "spectra_gemv_pf_plan": (c_int, [c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p]),
     "spectra_gemm_small_m_plan": (c_int, [c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p]),
+    "spectra_gemm_plan": (c_int, [c_int64, c_int64, c_int64, c_int64, c_void_p]),
+    "spectra_gemm_pair_capacity": (c_int, [c_void_p]),
     "spectra_w4a16_gemm_noalloc": (c_int, [
         c_void_p, c_int, c_int64,                      # a, a_dtype, a_row_stride
         c_void_p, c_int64,                             # packed, w_row_stride

@@ -92,6 +92,14 @@ bool sz_tma_enabled() {
   return on;
 }
 
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SPECTRA_B200_GEMM_PAIR");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 }  // namespace spectra
 
 using namespace spectra;
@@ -468,6 +476,21 @@ int spectra_fwht(const void* x, int x_dtype, int64_t x_row_stride, void* y, int 
   a.M = M; a.n = int(n); a.normalize = normalize ? 1 : 0;
   a.inv_norm = float(std::sqrt(double(n)));  // the divisor, as the reference's res / math.sqrt(d)
   return launch_fwht(a, static_cast<cudaStream_t>(stream));
+}
+
+int spectra_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t n_out, int64_t* out) {
+  if (!out) return SPECTRA_ERR_NULL_POINTER;
+  if (M <= 0 || N <= 0 || K <= 0 || n_out < 0 || M > 2147483647LL || N > 2147483647LL || K > 2147483647LL)
+    return SPECTRA_ERR_SHAPE;
+  const GemmPlan pl = plan_gemm(M, N, K, n_out);
+  out[0] = pl.MT; out[1] = pl.m_chunks; out[2] = pl.tiles_n; out[3] = pl.S; out[4] = pl.pair ? 1 : 0;
+  out[5] = int64_t(pl.tiles_pad) * pl.S; out[6] = pl.act_stages; out[7] = int64_t(pl.workspace);
+  return SPECTRA_OK;
+}
+
+int spectra_gemm_pair_capacity(int* clusters) {
+  if (!clusters) return SPECTRA_ERR_NULL_POINTER;
+  return gemm_pair_capacity(clusters);
 }
 
 size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t n_out) {

@@ -38,6 +38,12 @@ bool pf_path_enabled();
 // (on unless SPECTRA_B200_GEMM_SZ_TMA=0, which forces the plain-load path).
 bool sz_tma_enabled();
 
+// GEMM token tiles of >= 128 on SM pairs (cta_group::2, one M=256 MMA over
+// two CTAs' TMEM, each CTA loading half of the tokens): off unless
+// SPECTRA_B200_GEMM_PAIR=1 (bit-identical results; on B200 it measured within
+// a few percent of the one-SM kernel either way).
+bool pair_enabled();
+
 inline int cuda_status(cudaError_t e) {
   if (e != cudaSuccess) {
     set_last_cuda_error(e);

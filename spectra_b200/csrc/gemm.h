@@ -24,17 +24,21 @@ struct GemmArgs {
 
 struct GemmPlan {
   int MT, m_chunks, tiles_n;
+  bool pair;                  // tiles on SM pairs (cta_group::2): MT >= 128
+  int tiles_pad;              // tiles_n, rounded up to even in pair mode (the last pair's odd CTA has no rows)
   int nk, ncs, n_os;          // 64-k MMA steps, 256-k code stages, 64-column outlier steps
   int S;                      // K splits per tile
   int act_stages, code_stages, act_stage_bytes;
   int issuers;                // warps issuing MMAs (each with its own accumulator)
-  int a_slots;                // TMEM A slots of one 256-k unit (2 or 3)
+  int a_slots;                // TMEM A slots of one 64-k step (32 columns each)
   uint32_t tmem_cols;
   size_t smem, workspace;
 };
 
 GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out);
 int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st);
+// Two-CTA clusters of the SM-pair kernel resident at once on the current device.
+int gemm_pair_capacity(int* clusters);
 
 // Small-M GEMM (M = 2..16) on the raw-code tensor-core step (gemv_mt.cu);
 // SPECTRA_ERR_UNSUPPORTED (nothing launched) when the arguments do not meet

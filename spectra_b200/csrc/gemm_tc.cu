@@ -35,6 +35,11 @@
 // few weight tiles to fill the GPU; the last CTA of a tile sums the fp32
 // partials in split order (deterministic) and resets the tile's counter for
 // the next call.
+// Optionally (SPECTRA_B200_GEMM_PAIR=1), token tiles of >= 128 run on SM pairs
+// (a cluster of two CTAs, cta_group::2): each CTA still dequantises its own
+// 128-row tile into its own TMEM but loads only half of the token tile, and
+// the even CTA issues one M = 256 MMA per K=16 slice for both.  Per SM this
+// halves the activation bytes fetched and the MMA instructions issued.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -106,7 +111,7 @@ struct GemmKParams {
   float* partials;  // [S][M][N] when S > 1
   int* counters;    // [tiles_n * m_chunks]
   int M, N, K, layout;
-  int MT, S, nk, ncs, n_os, tiles_n;
+  int MT, S, nk, ncs, n_os, tiles_n, tiles_pad;
   int act_stages, code_stages, issuers, a_slots;
   uint32_t idesc, tmem_cols;
   int off_act, act_stage_bytes, off_code, off_sz, off_oidx, off_bar;
@@ -232,7 +237,7 @@ __device__ __forceinline__ uint16_t load_act16(const void* a, int64_t i) {
   return __ldg(reinterpret_cast<const unsigned short*>(a) + i);
 }
 
-template <bool BF16, bool SZ_TMA>
+template <bool BF16, bool SZ_TMA, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w4a16_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
                          const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_a,
@@ -259,11 +264,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x % kp.tiles_n;
-  const int split = blockIdx.x / kp.tiles_n;
+  const int tile = blockIdx.x % kp.tiles_pad;
+  const int split = blockIdx.x / kp.tiles_pad;
   const int mchunk = blockIdx.y;
   const int n0 = tile * kRows;
   const int m0 = mchunk * kp.MT;
+  // Pair mode: clusters of two CTAs (consecutive blockIdx.x: tiles 2i and
+  // 2i+1 of the same split).  Each CTA dequantises its own 128 weight rows
+  // into its own TMEM and loads half of the token tile (tokens m_own ..
+  // m_own + mt_local - 1) into its own act ring; rank 0 issues one M = 256
+  // MMA per K=16 slice for both and commits to the barriers of both.
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool issuer_cta = rank == 0;
+  const int mt_local = PAIR ? kp.MT / 2 : kp.MT;
+  const int m_own = m0 + int(rank) * mt_local;
   // This split's code stages [cs0, cs1) (balanced, never empty since S <= ncs)
   // and its main 64-k steps, then (last split only) the outlier steps.  The
   // unit of work between the dequant warps and the MMA issuers is one code
@@ -313,7 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(afull + i, 1);
       mbar_init(afree + i, NI);  // one commit per MMA issuer
     }
-    for (int i = 0; i < NAS; ++i) mbar_init(aready + i, kDeqWarps);
+    // pair mode: the dequant warps of both CTAs arrive on rank 0's barrier
+    for (int i = 0; i < NAS; ++i) mbar_init(aready + i, PAIR ? 2 * kDeqWarps : kDeqWarps);
     for (int i = 0; i < kDone; ++i) mbar_init(mdone + i, NI);  // one commit per MMA issuer
     mbar_init(accf, NI);
     fence_mbar_init();
@@ -327,6 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&map_a);
   }
   __syncthreads();
+  // the peer arrives on (and its copies complete on) this CTA's barriers:
+  // both CTAs' barriers are initialised before either goes on
+  if constexpr (PAIR) cluster_sync_all();
 
   // weight producer (warp 0, lane 0): code stage lc -> slot ring.idx, preceded
   // by its sz chunk when lc starts one.  Returns false if a wait gave up.
@@ -362,8 +380,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // TMEM is taken only after the wait, so a CTA waiting on the previous grid
   // never holds tensor memory that grid's CTAs could need.
   if (warp == 1) {
-    tmem_alloc(&s_tmem, kp.tmem_cols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&s_tmem, kp.tmem_cols);  // the same columns in both SMs
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&s_tmem, kp.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -416,8 +439,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         if (st >= n_out_st) {
-          mbar_arrive_expect_tx(afull + sa, act_bytes);
-          tma_load_2d(act_st + sa * act_bytes, &map_a, (st0 + st - n_out_st) * kStep, m0, afull + sa);
+          const int kx = (st0 + st - n_out_st) * kStep;
+          if constexpr (PAIR) {
+            // both halves complete on rank 0's barrier; rank 1's own barrier
+            // is only stepped, so that its phases keep counting steps (its
+            // dequant warps wait on it for the outlier steps)
+            if (issuer_cta)
+              mbar_arrive_expect_tx(afull + sa, 2u * act_bytes);
+            else
+              mbar_arrive(afull + sa);
+            tma_load_2d_pair(act_st + sa * act_bytes, &map_a, kx, m_own, cluster_addr(afull + sa, 0));
+          } else {
+            mbar_arrive_expect_tx(afull + sa, act_bytes);
+            tma_load_2d(act_st + sa * act_bytes, &map_a, kx, m0, afull + sa);
+          }
         } else {
           mbar_arrive(afull + sa);  // outlier step: the dequant warps fill the slot
         }
@@ -434,13 +469,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // they are spread over several warps, each accumulating its own K-slice
     // (k16 = issuer, issuer + NI, ...) into its own accumulator.
     const int issuer = warp == 1 ? 0 : warp - kActWarp;
-    if (issuer < NI && lane == 0) {
+    if (issuer < NI && lane == 0 && issuer_cta) {
       const uint32_t d_tmem = tmem + uint32_t(issuer * kp.MT);
+      // pair mode: every completion is signalled to the same barrier in both CTAs
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          mma_commit_pair(cluster_addr(bar, 0));
+          mma_commit_pair(cluster_addr(bar, 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
+      auto mma = [&](uint32_t d, uint32_t a_t, uint64_t b, uint32_t acc) {
+        if constexpr (PAIR)
+          mma_ts_pair(d, a_t, b, kp.idesc, acc);
+        else
+          mma_ts(d, a_t, b, kp.idesc, acc);
+      };
       bool live = true;
       Ring ar(AS), asl(NAS);
       for (int u = 0; u < n_units && live; ++u, asl.next()) {
         const int ns = steps_of(u);
-        if (!mbar_wait(aready + asl.idx, asl.phase, &s_abort)) {
+        // (rank 1's dequant warps arrive on it from the other SM: cluster-scope acquire)
+        const bool a_ok = PAIR ? mbar_wait_cluster(aready + asl.idx, asl.phase, &s_abort)
+                               : mbar_wait(aready + asl.idx, asl.phase, &s_abort);
+        if (!a_ok) {
           s_abort = 1;
           atomicAdd(&g_gemm_timeouts, 1);
           live = false;
@@ -468,11 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_base = smem_u32(act_st + slot[j] * act_bytes);
             for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
               const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
-              mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
-                     (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+              mma(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
             }
           }
-          for (int j = 0; j < ns; ++j) mma_commit(afree + slot[j]);
+          for (int j = 0; j < ns; ++j) commit(afree + slot[j]);
         } else {
           // fewer act slots than steps in a unit: release each slot after its
           // own step, or the producer could never fill the unit's last step
@@ -487,16 +539,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_base = smem_u32(act_st + ar.idx * act_bytes);
             for (int k16 = issuer; k16 < kStep / 16; k16 += NI) {
               const uint64_t bdesc = smem_desc_k_sw128(b_base + k16 * 32);
-              mma_ts(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, kp.idesc,
-                     (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
+              mma(d_tmem, a_unit + uint32_t(j * 32 + k16 * 8), bdesc, (u > 0 || j > 0 || k16 > issuer) ? 1u : 0u);
             }
-            mma_commit(afree + ar.idx);
+            commit(afree + ar.idx);
           }
         }
         if (!live) break;
-        mma_commit(mdone + u % kDone);
+        commit(mdone + u % kDone);
       }
-      mma_commit(accf);
+      commit(accf);
     }
   } else {
     // ---------------------------------------------------------------- dequant + epilogue
@@ -524,7 +575,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(aready + asl.idx);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(cluster_addr(aready + asl.idx, 0));  // the issuing CTA's barrier
+        else
+          mbar_arrive(aready + asl.idx);
+      }
       asl.next();
     };
 
@@ -603,24 +659,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) vals[half * 8 + cc] = pack2<BF16>(ov[2 * cc], ov[2 * cc + 1]);
         }
-        // gather a[m0+m, idx[j0+jj]] into the act slot, 128B-swizzled K-major;
-        // 8 independent loads in flight per thread
+        // gather a[m_own+m, idx[j0+jj]] into the act slot (this CTA's tokens),
+        // 128B-swizzled K-major; 8 independent loads in flight per thread
         uint8_t* bst = act_slot(u, j);
         const int tid_d = (warp - 2) * 32 + lane;
         constexpr int kBatch = 8;
-        for (int e0 = tid_d; e0 < kp.MT * kStep; e0 += kDeqWarps * 32 * kBatch) {
+        const int n_el = mt_local * kStep;
+        for (int e0 = tid_d; e0 < n_el; e0 += kDeqWarps * 32 * kBatch) {
           uint16_t v[kBatch];
 #pragma unroll
           for (int i = 0; i < kBatch; ++i) {
             const int e = e0 + i * kDeqWarps * 32;
             const int m = e / kStep, jj = e % kStep;
-            const int k = e < kp.MT * kStep ? oidx[jl * kStep + jj] : -1;
-            v[i] = (k >= 0 && m0 + m < kp.M) ? load_act16(kp.a, int64_t(m0 + m) * kp.a_rs + k) : uint16_t(0);
+            const int k = e < n_el ? oidx[jl * kStep + jj] : -1;
+            v[i] = (k >= 0 && m_own + m < kp.M) ? load_act16(kp.a, int64_t(m_own + m) * kp.a_rs + k) : uint16_t(0);
           }
 #pragma unroll
           for (int i = 0; i < kBatch; ++i) {
             const int e = e0 + i * kDeqWarps * 32;
-            if (e < kp.MT * kStep) {
+            if (e < n_el) {
               const int m = e / kStep, jj = e % kStep;
               const int chunk = (jj >> 3) ^ (m & 7);
               *reinterpret_cast<uint16_t*>(bst + m * 128 + chunk * 16 + (jj & 7) * 2) = v[i];
@@ -779,8 +836,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // split-K: the last CTA of this (tile, m-chunk) sums the partials in split
-  // order (deterministic)
-  if (kp.S > 1) {
+  // order (deterministic).  (The rowless CTA that pads an odd tile count in
+  // pair mode has no partials and no counter.)
+  if (kp.S > 1 && n0 < kp.N) {
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -859,7 +917,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if constexpr (PAIR) {
+    // Neither CTA frees its TMEM or leaves before both are done: rank 0's
+    // MMAs read rank 1's shared memory and TMEM, and rank 1's copies and
+    // arrivals land on rank 0's barriers.
+    cluster_sync_all();
+    if (warp == 1) {
+      __syncwarp();
+      tc_fence_after();
+      tmem_dealloc_pair(tmem, kp.tmem_cols);
+    }
+    cluster_sync_all();
+  } else if (warp == 1) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kp.tmem_cols);
@@ -887,16 +956,22 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.m_chunks = int((M + kMaxMT - 1) / kMaxMT);
   if (p.m_chunks > 1) p.MT = kMaxMT;
   p.tiles_n = int((N + kRows - 1) / kRows);
+  // SM pairs for token tiles of >= 128: the pair MMA's N (the whole token
+  // tile) is a multiple of 32, each CTA loads half of it
+  p.pair = pair_enabled() && p.MT >= 128;
+  if (p.pair) p.MT = (p.MT + 31) / 32 * 32;
+  p.tiles_pad = p.pair ? (p.tiles_n + 1) & ~1 : p.tiles_n;
+  const int mt_local = p.pair ? p.MT / 2 : p.MT;
   p.nk = int((K + kStep - 1) / kStep);
   p.ncs = int((K + kCodeK - 1) / kCodeK);
   p.n_os = int((n_out + kStep - 1) / kStep);
   const int sms = 148;  // B200; one CTA per SM (~200 KB of shared memory)
-  const int64_t ctas = int64_t(p.tiles_n) * p.m_chunks;
+  const int64_t ctas = int64_t(p.tiles_pad) * p.m_chunks;
   // split K so that all CTAs fit in ONE wave: rounding up (e.g. 32 tiles x 5 =
   // 160 CTAs) leaves a second wave of a few CTAs that doubles the time
   p.S = int(std::min<int64_t>(std::max<int64_t>(1, sms / ctas), p.ncs));
-  p.act_stage_bytes = p.MT * 128;
-  p.code_stages = p.MT <= 32 ? 6 : p.MT <= 64 ? 5 : p.MT <= 128 ? 4 : 3;
+  p.act_stage_bytes = mt_local * 128;
+  p.code_stages = mt_local <= 32 ? 6 : mt_local <= 64 ? 5 : mt_local <= 128 ? 4 : 3;
   const size_t fixed = 1024 + 64 + size_t(2 * kSzSlots + 3 + kDone + 1) * 8 + size_t(kSzSlots) * kSzSlot +
                        size_t(p.n_os) * kStep * 4;  // + outlier column indices
   const size_t code = size_t(p.code_stages) * (kCodeBytes + 16);
@@ -913,9 +988,9 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
 
 namespace {
 
-template <bool BF16, bool SZ_TMA>
+template <bool BF16, bool SZ_TMA, bool PAIR>
 int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmKParams& kp, cudaStream_t st) {
-  auto kern = gemm_w4a16_tc_kernel<BF16, SZ_TMA>;
+  auto kern = gemm_w4a16_tc_kernel<BF16, SZ_TMA, PAIR>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
@@ -924,15 +999,22 @@ int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmK
   e = attrs.run(dev, [&] { return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem)); });
   if (e != cudaSuccess) return cuda_status(e);
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(pl.tiles_n * pl.S), unsigned(pl.m_chunks));
+  cfg.gridDim = dim3(unsigned(pl.tiles_pad * pl.S), unsigned(pl.m_chunks));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if constexpr (PAIR) {  // consecutive blockIdx.x in clusters of two
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], kp));
 }
 
@@ -978,7 +1060,8 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   {
     cuuint64_t dims[2] = {cuuint64_t(a.K), cuuint64_t(a.M)};
     cuuint64_t strides[1] = {cuuint64_t(a.a_rs) * 2};
-    cuuint32_t box[2] = {kStep, cuuint32_t(pl.MT)}, es[2] = {1, 1};
+    // pair mode: each CTA of a pair fetches half of the token tile
+    cuuint32_t box[2] = {kStep, cuuint32_t(pl.pair ? pl.MT / 2 : pl.MT)}, es[2] = {1, 1};
     if (enc(&maps[3], bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
             const_cast<void*>(a.a), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -994,9 +1077,10 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.c = a.c; kp.c_dtype = a.c_dtype; kp.c_rs = a.c_rs;
   kp.M = a.M; kp.N = a.N; kp.K = a.K; kp.layout = a.layout;
   kp.MT = pl.MT; kp.S = pl.S; kp.nk = pl.nk; kp.ncs = pl.ncs; kp.n_os = pl.n_os; kp.tiles_n = pl.tiles_n;
+  kp.tiles_pad = pl.tiles_pad;
   kp.act_stages = pl.act_stages; kp.code_stages = pl.code_stages; kp.issuers = pl.issuers;
   kp.a_slots = pl.a_slots;
-  kp.idesc = idesc_f16(bf16, kRows, pl.MT);
+  kp.idesc = idesc_f16(bf16, pl.pair ? 2 * kRows : kRows, pl.MT);  // M = 256 over a pair
   kp.tmem_cols = pl.tmem_cols;
   kp.act_stage_bytes = pl.act_stage_bytes;
   // shared memory: act slots | code slots | sz slots | barriers (all 1024-aligned
@@ -1011,8 +1095,14 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
     kp.counters = reinterpret_cast<int*>(ws);
     kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + cnt_bytes);
   }
-  if (bf16) return sz_tma ? launch_variant<true, true>(pl, maps, kp, st) : launch_variant<true, false>(pl, maps, kp, st);
-  return sz_tma ? launch_variant<false, true>(pl, maps, kp, st) : launch_variant<false, false>(pl, maps, kp, st);
+  if (pl.pair) {
+    if (bf16)
+      return sz_tma ? launch_variant<true, true, true>(pl, maps, kp, st) : launch_variant<true, false, true>(pl, maps, kp, st);
+    return sz_tma ? launch_variant<false, true, true>(pl, maps, kp, st) : launch_variant<false, false, true>(pl, maps, kp, st);
+  }
+  if (bf16)
+    return sz_tma ? launch_variant<true, true, false>(pl, maps, kp, st) : launch_variant<true, false, false>(pl, maps, kp, st);
+  return sz_tma ? launch_variant<false, true, false>(pl, maps, kp, st) : launch_variant<false, false, false>(pl, maps, kp, st);
 }
 
 int gemm_noalloc_scratch(void** ptr, size_t* bytes) {
@@ -1041,5 +1131,23 @@ int gemm_noalloc_scratch(void** ptr, size_t* bytes) {
 }
 
 int gemm_timeouts(long long* out, bool reset) { return read_timeout_counter(g_gemm_timeouts, out, reset); }
+
+int gemm_pair_capacity(int* clusters) {
+  auto kern = gemm_w4a16_tc_kernel<true, true, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMaxDynSmem));
+  if (e != cudaSuccess) return cuda_status(e);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kMaxDynSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaOccupancyMaxActiveClusters(clusters, kern, &cfg));
+}
 
 }  // namespace spectra
