@@ -222,7 +222,7 @@ int spectra_w4a16_gemm(
   g.M = int(M); g.N = int(N); g.K = int(K); g.layout = layout;
   {  // the workspace contract does not depend on which kernel runs: checked first, on the host
     const GemmPlan pl = plan_gemm(M, N, K, n_out);
-    if (pl.S > 1 && (workspace == nullptr || workspace_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
+    if (pl.workspace > 0 && (workspace == nullptr || workspace_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
   }
   if (M <= 16) {  // decode batch sizes: the raw-code small-M kernel when its layout conditions hold
     const int r = launch_gemv_mt(g, static_cast<cudaStream_t>(stream));

@@ -81,6 +81,12 @@ constexpr int kMaxMT = 256;
 constexpr int kDone = 8;                             // units tracked by the MMA-done barrier ring
 constexpr int kMaxActStages = 16;
 constexpr size_t kMaxDynSmem = 200 * 1024;
+// Workspace layout: split-K tile counters in the first kCounterBytes (K is
+// split only when a wave holds >= 2 CTAs per tile, i.e. <= 74 tiles), the
+// fp32 partials after them, the gathered outlier activations after those.
+// The counter region is the same for every call, so no call's other regions
+// overwrite counters another call sharing the workspace relies on being zero.
+constexpr size_t kCounterBytes = 1024;
 
 __device__ int g_gemm_timeouts;  // stuck pipeline waits since load (diagnostic)
 
@@ -115,7 +121,41 @@ struct GemmKParams {
   int act_stages, code_stages, issuers, a_slots;
   uint32_t idesc, tmem_cols;
   int off_act, act_stage_bytes, off_code, off_sz, off_oidx, off_bar;
+  int pregather;  // outlier steps' activations come from the gathered tile (map_g) by TMA
 };
+
+// a[:, idx] for every token, gathered once per call into the compact tile
+// g[M][cols] (cols = 64 per outlier step; zero where an outlier column is
+// padding or out of range), which the GEMM then loads by tensor map like any
+// activation step.  Each CTA of the GEMM gathering it for itself would repeat
+// the same scattered loads once per weight tile (~8 us at 256 tokens).
+// Thread = 8 consecutive columns of one token: eight 2-byte loads, one
+// 16-byte store.  The indices are constants of the weights (loaded before the
+// dependency wait); a may be the previous kernel's output (loaded after it).
+__global__ void gather_outlier_acts_kernel(const uint16_t* __restrict__ a, int64_t a_rs, const void* idx, int idx_dtype,
+                                           int n_out, int K, int M, int cols, uint16_t* __restrict__ g) {
+  pdl_trigger();  // the GEMM may start its weight prefetch now
+  const int per_row = cols / 8;
+  const int64_t e = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= int64_t(M) * per_row) return;
+  const int m = int(e / per_row), j0 = int(e % per_row) * 8;
+  int k[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t kk = j0 + i < n_out ? load_index(idx, j0 + i, idx_dtype) : -1;
+    k[i] = (kk >= 0 && kk < K) ? int(kk) : -1;
+  }
+  pdl_wait();
+  uint32_t v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = k[i] >= 0 ? __ldg(a + int64_t(m) * a_rs + k[i]) : 0u;
+  uint4 o;
+  o.x = v[0] | (v[1] << 16);
+  o.y = v[2] | (v[3] << 16);
+  o.z = v[4] | (v[5] << 16);
+  o.w = v[6] | (v[7] << 16);
+  *reinterpret_cast<uint4*>(g + int64_t(m) * cols + j0) = o;
+}
 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
@@ -241,6 +281,7 @@ template <bool BF16, bool SZ_TMA, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w4a16_tc_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_s,
                          const __grid_constant__ CUtensorMap map_z, const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_g,
                          const __grid_constant__ GemmKParams kp) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -340,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&map_z);
     }
     prefetch_tensormap(&map_a);
+    if (kp.pregather) prefetch_tensormap(&map_g);
   }
   __syncthreads();
   // the peer arrives on (and its copies complete on) this CTA's barriers:
@@ -438,8 +480,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           atomicAdd(&g_gemm_timeouts, 1);
           break;
         }
-        if (st >= n_out_st) {
-          const int kx = (st0 + st - n_out_st) * kStep;
+        if (st >= n_out_st || kp.pregather) {
+          // a main step: activations at k; an outlier step with the gathered
+          // tile: its 64 columns of that tile
+          const bool main_step = st >= n_out_st;
+          const CUtensorMap* map = main_step ? &map_a : &map_g;
+          const int kx = main_step ? (st0 + st - n_out_st) * kStep : ostep(st) * kStep;
           if constexpr (PAIR) {
             // both halves complete on rank 0's barrier; rank 1's own barrier
             // is only stepped, so that its phases keep counting steps (its
@@ -448,13 +494,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_expect_tx(afull + sa, 2u * act_bytes);
             else
               mbar_arrive(afull + sa);
-            tma_load_2d_pair(act_st + sa * act_bytes, &map_a, kx, m_own, cluster_addr(afull + sa, 0));
+            tma_load_2d_pair(act_st + sa * act_bytes, map, kx, m_own, cluster_addr(afull + sa, 0));
           } else {
             mbar_arrive_expect_tx(afull + sa, act_bytes);
-            tma_load_2d(act_st + sa * act_bytes, &map_a, kx, m0, afull + sa);
+            tma_load_2d(act_st + sa * act_bytes, map, kx, m0, afull + sa);
           }
         } else {
-          mbar_arrive(afull + sa);  // outlier step: the dequant warps fill the slot
+          mbar_arrive(afull + sa);  // outlier step: the dequant warps gather into the slot
         }
         issued = st + 1;
       }
@@ -604,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // outlier column indices of this CTA's outlier steps, once (the gather of
     // a[:, idx] then needs a single dependent load per element)
-    if (n_out_st > 0) {
+    if (n_out_st > 0 && !kp.pregather) {
       const int tid_d = (warp - 2) * 32 + lane;
       for (int j = tid_d; j < n_out_st * kStep; j += kDeqWarps * 32) {
         const int jg = ostep(j / kStep) * kStep + j % kStep;  // outlier column
@@ -619,7 +665,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = 0; u < n_ou && alive; ++u) {
       bool ok = u < NAS || wait_all(mdone + (u - NAS) % kDone, done_parity(u - NAS));
       const int ns = steps_of(u);
-      for (int j = 0; j < ns && ok; ++j) {
+      // the act slots: free for the gather (or filled by the producer's copy
+      // of the gathered tile, which only the MMA issuer waits for)
+      for (int j = 0; j < ns && ok && !kp.pregather; ++j) {
         const int st = step_of(u, j);
         ok = wait_all(afull + st % AS, uint32_t((st / AS) & 1));
       }
@@ -665,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tid_d = (warp - 2) * 32 + lane;
         constexpr int kBatch = 8;
         const int n_el = mt_local * kStep;
-        for (int e0 = tid_d; e0 < n_el; e0 += kDeqWarps * 32 * kBatch) {
+        for (int e0 = tid_d; e0 < (kp.pregather ? 0 : n_el); e0 += kDeqWarps * 32 * kBatch) {
           uint16_t v[kBatch];
 #pragma unroll
           for (int i = 0; i < kBatch; ++i) {
@@ -982,14 +1030,21 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   p.a_slots = p.issuers * p.MT + 3 * 128 <= 512 ? 3 : 2;
   p.tmem_cols = 32;
   while (p.tmem_cols < uint32_t(p.issuers * p.MT + p.a_slots * 128)) p.tmem_cols <<= 1;
-  p.workspace = p.S > 1 ? (256 * ((size_t(p.tiles_n) * p.m_chunks * 4 + 255) / 256) + size_t(p.S) * M * N * 4) : 0;
+  p.partials_off = kCounterBytes;
+  p.workspace = p.S > 1 ? kCounterBytes + size_t(p.S) * M * N * 4 : 0;
+  // Token tiles of >= 128: the outlier columns' activations are gathered once
+  // per call into the workspace (after the split-K region, never over the
+  // counters) instead of once per weight tile.
+  p.pregather = n_out > 0 && p.MT >= 128;
+  p.gather_off = 256 * ((std::max(p.workspace, kCounterBytes) + 255) / 256);
+  if (p.pregather) p.workspace = p.gather_off + 256 * ((size_t(M) * p.n_os * kStep * 2 + 255) / 256);
   return p;
 }
 
 namespace {
 
 template <bool BF16, bool SZ_TMA, bool PAIR>
-int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmKParams& kp, cudaStream_t st) {
+int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[5], const GemmKParams& kp, cudaStream_t st) {
   auto kern = gemm_w4a16_tc_kernel<BF16, SZ_TMA, PAIR>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1015,7 +1070,7 @@ int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmK
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], kp));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], maps[4], kp));
 }
 
 }  // namespace
@@ -1023,13 +1078,14 @@ int launch_variant(const GemmPlan& pl, const CUtensorMap (&maps)[4], const GemmK
 int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   const GemmPlan pl = plan_gemm(a.M, a.N, a.K, a.n_out);
   if (pl.tmem_cols > 512 || pl.smem > kMaxDynSmem || pl.act_stages < 3) return SPECTRA_ERR_UNSUPPORTED;
-  if (pl.S > 1 && (ws == nullptr || ws_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
+  if (pl.workspace > 0 && (ws == nullptr || ws_bytes < pl.workspace)) return SPECTRA_ERR_WORKSPACE;
+  if (pl.S > 1 && size_t(pl.tiles_n) * pl.m_chunks * 4 > kCounterBytes) return SPECTRA_ERR_UNSUPPORTED;
   auto enc = tensor_map_encoder();
   if (!enc) return SPECTRA_ERR_UNSUPPORTED;
   const bool bf16 = a.a_dtype == SPECTRA_DT_BF16;
   const int G = a.K / kGroup;
 
-  CUtensorMap maps[4];  // codes, scales, zero points, activations
+  CUtensorMap maps[5];  // codes, scales, zero points, activations, gathered outlier activations
   memset(maps, 0, sizeof(maps));
   {
     cuuint64_t dims[2] = {cuuint64_t(a.K / 2), cuuint64_t(a.N)};
@@ -1068,6 +1124,18 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
       return SPECTRA_ERR_ALIGNMENT;
   }
 
+  uint16_t* gathered = pl.pregather ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(ws) + pl.gather_off) : nullptr;
+  if (pl.pregather) {
+    const int cols = pl.n_os * kStep;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(a.M)};
+    cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+    cuuint32_t box[2] = {kStep, cuuint32_t(pl.pair ? pl.MT / 2 : pl.MT)}, es[2] = {1, 1};
+    if (enc(&maps[4], bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, gathered, dims,
+            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return SPECTRA_ERR_ALIGNMENT;
+  }
+
   GemmKParams kp{};
   kp.scales = a.scales; kp.s_rs = a.s_rs; kp.s_cs = a.s_cs;
   kp.zeros = a.zeros; kp.z_rs = a.z_rs; kp.z_cs = a.z_cs;
@@ -1078,6 +1146,7 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.M = a.M; kp.N = a.N; kp.K = a.K; kp.layout = a.layout;
   kp.MT = pl.MT; kp.S = pl.S; kp.nk = pl.nk; kp.ncs = pl.ncs; kp.n_os = pl.n_os; kp.tiles_n = pl.tiles_n;
   kp.tiles_pad = pl.tiles_pad;
+  kp.pregather = pl.pregather ? 1 : 0;
   kp.act_stages = pl.act_stages; kp.code_stages = pl.code_stages; kp.issuers = pl.issuers;
   kp.a_slots = pl.a_slots;
   kp.idesc = idesc_f16(bf16, pl.pair ? 2 * kRows : kRows, pl.MT);  // M = 256 over a pair
@@ -1091,9 +1160,24 @@ int launch_gemm(const GemmArgs& a, void* ws, size_t ws_bytes, cudaStream_t st) {
   kp.off_oidx = kp.off_sz + kSzSlots * kSzSlot;
   kp.off_bar = kp.off_oidx + pl.n_os * kStep * 4;
   if (pl.S > 1) {
-    const size_t cnt_bytes = 256 * ((size_t(pl.tiles_n) * pl.m_chunks * 4 + 255) / 256);
     kp.counters = reinterpret_cast<int*>(ws);
-    kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + cnt_bytes);
+    kp.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.partials_off);
+  }
+  if (pl.pregather) {
+    const int cols = pl.n_os * kStep;
+    const int64_t threads = int64_t(a.M) * (cols / 8);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gather_outlier_acts_kernel, static_cast<const uint16_t*>(a.a),
+                                             int64_t(a.a_rs), a.idx, a.idx_dtype, a.n_out, a.K, a.M, cols, gathered);
+    if (e != cudaSuccess) return cuda_status(e);
   }
   if (pl.pair) {
     if (bf16)

@@ -143,6 +143,18 @@ def test_gemm_token_counts(M, dt):
     check(fmt, act(M, 1024, seed=M, dtype=dt), what=f"M={M} {dt}")
 
 
+def test_workspace_shared_by_outlier_gather_and_split_k():
+    """A call that gathers its outlier activations into the workspace (256
+    tokens, 75 weight tiles: K not split) and a split-K call after it on the
+    same stream share one workspace: the second call's tile counters must
+    still be zero, and its result exact."""
+    big = random_format(9600, 512, 21, seed=1, ow_dtype="bf16")
+    check(big, act(256, 512, seed=2, dtype="bf16"), what="gathering call")
+    fmt = random_format(640, 1024, 21, seed=17, ow_dtype="bf16")
+    check(fmt, act(17, 1024, seed=17, dtype="bf16"), what="split-K call after it")
+    check(big, act(256, 512, seed=3, dtype="bf16"), what="gathering call after it")
+
+
 @pytest.mark.parametrize("M", [257, 300, 600])
 def test_gemm_several_token_chunks(M):
     fmt = random_format(384, 512, 5, seed=M, ow_dtype="bf16")
