@@ -1094,6 +1094,25 @@ def run_gpu(args, world, rank, local):
             step_graphs[i % N_COPIES].replay()
             h_out_all.copy_(d_out_all, non_blocking=True)
 
+    # The same per-step work with the copies inside the graph too: `steps`
+    # steps of (pinned H2D memcpy node, the seven public-API calls, D2H memcpy
+    # node of all outputs) in one CUDA graph, as a server that captures its
+    # whole decode step would run it -- no host launch cost between steps.
+    def e2e_in_graph_fn(n):
+        def run():
+            for i in range(n):
+                d_in_all.copy_(h_in_all, non_blocking=True)
+                run_layer(SK, layers[i % N_COPIES], d_in, d_out)
+                h_out_all.copy_(d_out_all, non_blocking=True)
+        return run
+    try:
+        e2e_g_timed = capture(e2e_in_graph_fn(args.steps), dev)
+        e2e_g_warm = capture(e2e_in_graph_fn(max(args.warmup, 1)), dev)
+        singles += [e2e_g_timed, e2e_g_warm]
+    except RuntimeError as exc:  # a torch build that cannot capture pinned copies
+        e2e_g_timed = e2e_g_warm = None
+        e2e_g_error = str(exc).splitlines()[0][:200]
+
     def e2e_eager_steps(n):
         for i in range(n):
             lay = layers[i % N_COPIES]
@@ -1112,6 +1131,17 @@ def run_gpu(args, world, rank, local):
     barrier(world)
     dt_e2e = max_over_ranks(dt_e2e, world, dev)
     e2e_value = bytes_step * args.steps * world / dt_e2e / 1e9
+    # every rank takes the same steps (the collective in max_over_ranks)
+    e2e_in_graph = None
+    if e2e_g_timed is not None:
+        for _ in range(3):
+            e2e_g_warm.replay()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        dt_g = time_events(lambda: e2e_g_timed.replay(), dev)
+        barrier(world)
+        dt_g = max_over_ranks(dt_g, world, dev)
+        e2e_in_graph = bytes_step * args.steps * world / dt_g / 1e9
     barrier(world)
     dt_eager = time_events(lambda: e2e_eager_steps(args.steps), dev)
     barrier(world)
@@ -1125,6 +1155,20 @@ def run_gpu(args, world, rank, local):
     torch.cuda.synchronize(dev)
     if not torch.equal(graph_out, h_out_all):
         raise RuntimeError("graph-replayed and eager layer outputs differ")
+    if e2e_g_timed is not None:  # and the all-in-graph run's last step (layer copy (steps-1) mod N_COPIES)
+        e2e_g_timed.replay()
+        torch.cuda.synchronize(dev)
+        in_graph_out = h_out_all.clone()
+        lay = layers[(args.steps - 1) % N_COPIES]
+        d_in_all.copy_(h_in_all)
+        for name, K, N in LAYER:
+            p, s_, z, idx, ow = lay[name]
+            SK.fused_w4a16_gemv_hdsq(d_in[INPUT_OF[name]], p, s_, z, outlier_idx=idx, outlier_w=ow,
+                                     out=d_out[name], marlin_layout=True)
+        h_out_all.copy_(d_out_all)
+        torch.cuda.synchronize(dev)
+        if not torch.equal(in_graph_out, h_out_all):
+            raise RuntimeError("all-in-graph and eager layer outputs differ")
 
     sweep = gemm_sweep(SK, dev) if not args.no_gemm_sweep else None
     ops = ops_sweep(dev) if not args.no_ops_sweep else None
@@ -1155,7 +1199,13 @@ def run_gpu(args, world, rank, local):
                            "all outputs"},
             "e2e_eager": {"value": round(eager_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                           "d2h_bytes_per_step": d2h, "how": "one Python API call per linear, no graph"},
-            "gpu_launches": 7 * args.steps * 3,  # value, e2e and e2e_eager timed regions
+            "e2e_copies_in_graph": ({"value": round(e2e_in_graph, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                                     "d2h_bytes_per_step": d2h,
+                                     "how": "the timed steps in one CUDA graph, each step a pinned H2D memcpy "
+                                            "node, the seven public-API calls and a D2H memcpy node"}
+                                    if e2e_in_graph is not None else {"unavailable": e2e_g_error}),
+            # value, e2e, e2e_eager and (when captured) e2e_copies_in_graph timed regions
+            "gpu_launches": 7 * args.steps * (4 if e2e_in_graph is not None else 3),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": GATE_TRAFFIC_BYTES,
                          "kernel": "gemv_pf_kernel gate_proj K=2048 N=8192 M=1", "peak_source": peak_kind,
