@@ -32,7 +32,7 @@ struct GemmPlan {
   int issuers;                // warps issuing MMAs (each with its own accumulator)
   int a_slots;                // TMEM A slots of one 256-k unit (2 or 3)
   uint32_t tmem_cols;
-  bool pregather;             // outlier activations gathered once per call (token tiles >= 128)
+  bool pregather;             // outlier activations gathered once per call (token tiles >= 32)
   size_t partials_off;        // workspace offset of the split-K partials (after the counters)
   size_t gather_off;          // workspace offset of the gathered tile [M][n_os * 64]
   size_t smem, workspace;

@@ -1032,10 +1032,12 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int64_t n_out) {
   while (p.tmem_cols < uint32_t(p.issuers * p.MT + p.a_slots * 128)) p.tmem_cols <<= 1;
   p.partials_off = kCounterBytes;
   p.workspace = p.S > 1 ? kCounterBytes + size_t(p.S) * M * N * 4 : 0;
-  // Token tiles of >= 128: the outlier columns' activations are gathered once
+  // Token tiles of >= 32: the outlier columns' activations are gathered once
   // per call into the workspace (after the split-K region, never over the
-  // counters) instead of once per weight tile.
-  p.pregather = n_out > 0 && p.MT >= 128;
+  // counters) instead of once per weight tile (measured equal at 32 tokens,
+  // faster from 64 on and with many outlier columns; at 16 tokens each CTA's
+  // share is too small to pay for the extra launch).
+  p.pregather = n_out > 0 && p.MT >= 32;
   p.gather_off = 256 * ((std::max(p.workspace, kCounterBytes) + 255) / 256);
   if (p.pregather) p.workspace = p.gather_off + 256 * ((size_t(M) * p.n_os * kStep * 2 + 255) / 256);
   return p;
