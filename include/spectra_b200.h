@@ -131,7 +131,9 @@ SPECTRA_API int spectra_w4a16_dequant(
  *   packed row n at packed + n*w_row_stride; base and row stride 16-byte aligned
  *   c      [M, N] at c + m*c_row_stride + n, c_dtype == a_dtype
  *   workspace: caller-owned device memory of at least
- *          spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out) bytes, zeroed once
+ *          spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out) bytes (split-K
+ *          counters and partials; from 17 tokens on with outlier columns, the
+ *          activations at those columns gathered once per call), zeroed once
  *          before its first use; every call leaves its counter region zero
  *          again.  Calls that share a workspace must not overlap in time.
  */
@@ -159,7 +161,8 @@ SPECTRA_API size_t spectra_w4a16_gemm_workspace_bytes(int64_t M, int64_t N, int6
  * like the reference's batched_w4a16_gemm signature (no workspace argument).
  *
  * Same arguments and results as spectra_w4a16_gemm, without the workspace:
- * split-K scratch lives in one file-scope device array of
+ * its scratch (split-K counters and partials, the gathered activations at the
+ * outlier columns) lives in one file-scope device array of
  * SPECTRA_GEMM_NOALLOC_SCRATCH_BYTES per device, and the call makes no
  * cudaMalloc/cudaFree or other allocating call.
  *   - Limit: a problem whose spectra_w4a16_gemm_workspace_bytes(M, N, K, n_out)
