@@ -16,9 +16,10 @@
 //      addresses, no TMA);
 //   2. after a CTA barrier, writes the call's epoch into flag (rank, b) of
 //      every peer (release, system scope: the barrier orders the CTA's stores
-//      before it);
+//      before it; lane r of warp 0 writes peer r's, all in one instruction);
 //   3. waits until flag (r, b) of its own buffer holds the epoch for every
-//      peer r (acquire, system scope; bounded by wait_limit_ns -- on time-out
+//      peer r (lane r polls peer r's; acquire, system scope; bounded by
+//      wait_limit_ns -- on time-out
 //      it counts the event in g_p2p_timeouts, read by spectra_device_timeouts,
 //      and returns), then copies chunk b of every rank's slice into the [M, N]
 //      output: this rank's from `src`, each peer's from its region.
@@ -82,15 +83,18 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_allgather_kernel(P2pArgs a) {
   }
   __syncthreads();
 
-  // 2./3. flag the chunk to every peer, then wait for theirs
-  if (threadIdx.x == 0) {
-    for (int r = 0; r < a.world; ++r)
-      if (r != a.rank) st_release_sys(reinterpret_cast<int*>(a.peer[r]) + a.rank * kP2pMaxCtas + b, epoch);
+  // 2./3. flag the chunk to every peer, then wait for theirs: lane r of warp 0
+  // serves peer r, so the world-1 release stores go out as one instruction
+  // (one system-scope fence for all peers, not one per peer in turn) and the
+  // peers' flags are polled side by side
+  if (threadIdx.x < 32) {
+    const int r = threadIdx.x;
+    const bool peer_lane = r < a.world && r != a.rank;
+    if (peer_lane) st_release_sys(reinterpret_cast<int*>(a.peer[r]) + a.rank * kP2pMaxCtas + b, epoch);
     const int* flags = reinterpret_cast<const int*>(a.peer[a.rank]);
-    int ok = 1;
-    uint64_t t0 = 0;
-    for (int r = 0; r < a.world && ok; ++r) {
-      if (r == a.rank) continue;
+    bool ok = true;
+    if (peer_lane) {
+      uint64_t t0 = 0;
       for (uint32_t polls = 1; int(unsigned(ld_acquire_sys(flags + r * kP2pMaxCtas + b)) - unsigned(epoch)) < 0;
            ++polls) {
         if ((polls & 63) == 0) {
@@ -98,14 +102,17 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_allgather_kernel(P2pArgs a) {
           if (t0 == 0) {
             t0 = now;
           } else if (now - t0 > a.wait_limit_ns) {
-            atomicAdd(&g_p2p_timeouts, 1);
-            ok = 0;
+            ok = false;
             break;
           }
         }
       }
     }
-    s_ok = ok;
+    ok = __all_sync(0xffffffffu, ok);
+    if (r == 0) {
+      if (!ok) atomicAdd(&g_p2p_timeouts, 1);  // once per CTA that gave up
+      s_ok = ok ? 1 : 0;
+    }
   }
   __syncthreads();
   if (!s_ok) return;  // output undefined; the host reads the counter between steps
