@@ -29,9 +29,11 @@
 //   MMA        : tcgen05.mma kind::f16, A from TMEM, B from shared memory,
 //                D (fp32, 128 lanes x MT columns) in TMEM; tcgen05.commit
 //                frees the act slot and the A slot.
-// Outlier columns become extra 64-column steps: the dequant warps gather
-// a[:, idx] into the act slot (same swizzled layout) and convert ow rows into
-// the A slot.  K is split across CTAs (in 256-k code stages) when there are too
+// Outlier columns become extra 64-column steps: the dequant warps convert ow
+// rows into the A slot; the activations a[:, idx] come from the tile that
+// gather_outlier_acts_kernel gathered once per call (token tiles >= 32, by
+// TMA like any step), or at 16 tokens the dequant warps gather them into the
+// act slot themselves (same swizzled layout).  K is split across CTAs (in 256-k code stages) when there are too
 // few weight tiles to fill the GPU; the last CTA of a tile sums the fp32
 // partials in split order (deterministic) and resets the tile's counter for
 // the next call.
